@@ -1,0 +1,68 @@
+/* tessera_b200_ops.h - per-kernel entry points of libtessera_b200.so, for
+ * parity tests of each stage of the forward pass against the CPU oracle.
+ *
+ * Every pointer is device memory of the current CUDA device; every call
+ * enqueues on `stream` (a cudaStream_t, NULL = legacy default stream) and
+ * returns 0, or -1 with a "tcb_op_...: message" line on stderr. bf16 arrays
+ * are passed as raw 16-bit storage (void *).
+ */
+#ifndef TESSERA_B200_OPS_H
+#define TESSERA_B200_OPS_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* out[M,N] = bf16([relu](A[M,K] W[N,K]^T + bias) + residual).
+ * Replaces the reference's Linear (src/tessera_cpu.cpp:215-243 make_linear,
+ * src/tessera_cuda.cu:438-445 gemm). Residual: res (pitch ldr), or the DOY
+ * sinusoid of pe_doy[row * pe_stride] looked up in pe_table (367 x 640 bf16,
+ * src/tessera_cpu.cpp:503-509) with pe_div (320 f32) for non-table days.
+ * bn = tile width (0 = automatic). */
+int tcb_op_gemm(const void *A, int lda, const void *W, const float *bias, int relu, const void *res, int ldr,
+                const float *pe_doy, int pe_stride, const void *pe_table, const float *pe_div, void *out, int ldo,
+                int M, int N, int K, int bn, int *status, void *stream);
+
+/* Valid-observation counts (src/tessera_encode.cpp:245-257) of pixels [p0, p0+np). */
+int tcb_op_count(const uint8_t *masks, const int16_t *asc, const int16_t *desc, int64_t T2, int64_t Ta, int64_t Td,
+                 int64_t N, int64_t p0, int64_t np, int32_t *n2, int32_t *n1, void *stream);
+
+/* Gather + pad + z-score of one modality (src/tessera_encode.cpp:281-329).
+ * bins[i] = rows of pixel i, off[i] = its first record (np + 1 entries);
+ * rec receives (sum bins, C+1) f32 records. */
+int tcb_op_gather(int modality, const uint16_t *bands, const uint8_t *masks, const uint16_t *doys,
+                  const int16_t *asc, const int16_t *asc_doy, const int16_t *desc, const int16_t *desc_doy,
+                  int64_t T2, int64_t Ta, int64_t Td, int64_t N, int64_t p0, int64_t np, const int32_t *bins,
+                  const int64_t *off, float *rec, void *stream);
+
+/* emb1: y = bf16(relu(bf16(rec[:, :C]) W1^T + b1)); w1t = W1^T as f32 (C x 640)
+ * (src/tessera_cpu.cpp:387-404). */
+int tcb_op_emb1(int C, const float *rec, int64_t M, const float *w1t, const float *b1, void *y, void *stream);
+
+/* Self-attention per pixel segment (src/tessera_cpu.cpp:333-352,410-418).
+ * off (npix+1 entries) or, when NULL, uniform segments of uniform_T tokens. */
+int tcb_op_attention(const void *qkv, const int64_t *off, int64_t uniform_T, int64_t npix, int Tmax, void *att,
+                     void *stream);
+
+/* LayerNorm over rows of 640 (src/tessera_cpu.cpp:245-263); g/b may be NULL. */
+int tcb_op_layernorm640(const void *x, int64_t M, const float *g, const float *b, void *y, void *stream);
+
+/* Attention pooling (src/tessera_cpu.cpp:434-455) into fused[:, col0:col0+640]. */
+int tcb_op_pool(const void *x, const int64_t *off, int64_t uniform_T, int64_t npix, const float *q, float qb,
+                void *fused, int col0, void *stream);
+
+/* Head LayerNorm(2560) + ReLU in place (src/tessera_cpu.cpp:568-571). */
+int tcb_op_ln_relu2560(void *r, int64_t P, const float *g, const float *b, void *stream);
+
+/* Final LayerNorm(128, no affine) -> bf16 -> f32 out, or int8 codes + scales
+ * (src/tessera_cpu.cpp:573-575, src/tessera_encode.cpp:344-361). */
+int tcb_op_out128(const void *r2, int64_t P, const uint8_t *empty, float *out, int8_t *codes, float *scales,
+                  void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TESSERA_B200_OPS_H */

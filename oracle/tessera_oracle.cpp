@@ -1,0 +1,435 @@
+// CPU ORACLE - TEST INFRASTRUCTURE ONLY.
+//
+// A plain C++17/OpenMP restatement of the reference's oneDNN CPU back end
+// (src/tessera_cpu.cpp of mtelvers/tessera-inference), exporting the same four
+// C symbols (tc_create / tc_encode / tc_profile_dump / tc_destroy) so that the
+// reference's own, unmodified driver (src/tessera_encode.cpp) links against it.
+// oneDNN v3.13.3, which the reference back end needs (README.md:24-38), is not
+// available on this machine; this file restates the arithmetic of the oneDNN
+// primitives the reference calls, at the same rounding points:
+//   Linear (make_linear, tessera_cpu.cpp:215-243): bf16 A and W, f32
+//     accumulation, + f32 bias, [ReLU], [+ bf16 residual in f32], one RNE
+//     rounding to bf16 (post-op order :220-222).
+//   Attention (:333-343, :410-418): S = bf16(f32(QK^T) * 1/sqrt(160));
+//     softmax_accurate in f32 (max-subtracted exp, sum, scaled by 1/sum) -> bf16;
+//     O = bf16(f32(P V)).
+//   LayerNorm (make_ln, :245-263): f32 mean and biased variance of the bf16
+//     row, (x - mean) / sqrt(var + 1e-5) * gamma + beta -> bf16.
+//   Pooling (:434-455) and head (:567-575): as written there.
+// Summation order: every dot product accumulates in index order with f32
+// FMA; products of two bf16 values are exact in f32, so FMA and a separate
+// multiply-add give the same result.
+//
+// Nothing in the product links, loads or runs this file: only tests/,
+// __graft_entry__.smoke() and bench.py's CPU-baseline leg use it, as the checker.
+//
+// TC_ORACLE_DUMP=DIR makes tc_encode write each call's inputs and outputs to
+// DIR/batch_NNNNN.bin (int64 G, T2, T1; f32 s2, s1, out), which is how the
+// reference driver's own batching, padding and standardisation are captured
+// as golden fixtures.
+#include <algorithm>
+#include <cmath>
+#include <cstdint>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include <omp.h>
+
+namespace {
+
+constexpr int64_t D = 640, NH = 4, HD = 160, FF = 2560, NL = 4, RED = 2560, OUT = 128;
+constexpr float LN_EPS = 1e-5f;
+
+inline uint16_t f2bf(float f) {  // round to nearest even (tessera_cpu.cpp:43-48)
+    uint32_t u;
+    std::memcpy(&u, &f, 4);
+    u += 0x7FFFu + ((u >> 16) & 1u);
+    return uint16_t(u >> 16);
+}
+inline float bf2f(uint16_t b) {
+    uint32_t u = uint32_t(b) << 16;
+    float f;
+    std::memcpy(&f, &u, 4);
+    return f;
+}
+inline float rbf(float f) { return bf2f(f2bf(f)); }
+
+struct Tensor {
+    std::vector<int64_t> shape;
+    std::vector<float> data;
+};
+
+std::map<std::string, Tensor> load_weights(const char *path) {  // .tcw, tessera_cpu.cpp:81-106
+    FILE *f = std::fopen(path, "rb");
+    if (!f) throw std::runtime_error(std::string("cannot open ") + path);
+    std::unique_ptr<FILE, int (*)(FILE *)> guard(f, std::fclose);
+    char magic[4];
+    uint32_t n;
+    if (std::fread(magic, 1, 4, f) != 4 || std::memcmp(magic, "TCW1", 4) || std::fread(&n, 4, 1, f) != 1)
+        throw std::runtime_error("bad weights file");
+    std::map<std::string, Tensor> w;
+    for (uint32_t i = 0; i < n; ++i) {
+        uint32_t len, nd;
+        if (std::fread(&len, 4, 1, f) != 1) throw std::runtime_error("truncated weights");
+        std::string name(len, '\0');
+        if (std::fread(name.data(), 1, len, f) != len || std::fread(&nd, 4, 1, f) != 1)
+            throw std::runtime_error("truncated weights");
+        Tensor t;
+        t.shape.resize(nd);
+        if (std::fread(t.shape.data(), 8, nd, f) != nd) throw std::runtime_error("truncated weights");
+        int64_t count = 1;
+        for (auto s : t.shape) count *= s;
+        t.data.resize(count);
+        if (std::fread(t.data.data(), 4, count, f) != size_t(count)) throw std::runtime_error("truncated weights");
+        w.emplace(std::move(name), std::move(t));
+    }
+    return w;
+}
+
+// Linear weights packed for the CPU kernel: f32 (exact bf16 values) in
+// column panels of 16: wp[(n/16)][k][16].
+struct Lin {
+    int64_t N = 0, K = 0;
+    std::vector<float> wp;
+    std::vector<float> bias;
+};
+
+Lin take_linear(std::map<std::string, Tensor> &W, const std::string &wn, const std::string &bn) {
+    const Tensor &t = W.at(wn);
+    Lin l;
+    l.N = t.shape[0];
+    l.K = t.shape[1];
+    if (l.N % 16) throw std::runtime_error("linear width not a multiple of 16: " + wn);
+    l.wp.resize(l.N * l.K);
+    for (int64_t n = 0; n < l.N; ++n)
+        for (int64_t k = 0; k < l.K; ++k)
+            l.wp[((n / 16) * l.K + k) * 16 + (n % 16)] = bf2f(f2bf(t.data[n * l.K + k]));
+    l.bias = W.at(bn).data;
+    return l;
+}
+
+typedef float v16 __attribute__((vector_size(64)));
+
+// y[M, N] = bf16([relu](A[M, K] W^T + b) [+ res]); A, res, y bf16 row-major.
+__attribute__((target_clones("arch=x86-64-v4", "default"))) void linear(const Lin &L, int64_t M, const uint16_t *A,
+                                                                         uint16_t *y, bool relu,
+                                                                         const uint16_t *res) {
+    const int64_t K = L.K, N = L.N;
+    std::vector<float> af(4 * K);
+    for (int64_t m0 = 0; m0 < M; m0 += 4) {
+        const int64_t mr = std::min<int64_t>(4, M - m0);
+        for (int64_t r = 0; r < 4; ++r)
+            for (int64_t k = 0; k < K; ++k) af[r * K + k] = r < mr ? bf2f(A[(m0 + r) * K + k]) : 0.f;
+        for (int64_t nb = 0; nb < N; nb += 32) {
+            const bool two = nb + 16 < N;
+            const float *p0 = L.wp.data() + (nb / 16) * K * 16;
+            const float *p1 = two ? p0 + K * 16 : p0;
+            v16 c00 = {}, c01 = {}, c10 = {}, c11 = {}, c20 = {}, c21 = {}, c30 = {}, c31 = {};
+            for (int64_t k = 0; k < K; ++k) {
+                v16 w0, w1;
+                std::memcpy(&w0, p0 + k * 16, 64);
+                std::memcpy(&w1, p1 + k * 16, 64);
+                const float a0 = af[k], a1 = af[K + k], a2 = af[2 * K + k], a3 = af[3 * K + k];
+                c00 += a0 * w0; c01 += a0 * w1;
+                c10 += a1 * w0; c11 += a1 * w1;
+                c20 += a2 * w0; c21 += a2 * w1;
+                c30 += a3 * w0; c31 += a3 * w1;
+            }
+            const v16 *cs[4][2] = {{&c00, &c01}, {&c10, &c11}, {&c20, &c21}, {&c30, &c31}};
+            for (int64_t r = 0; r < mr; ++r)
+                for (int h = 0; h < (two ? 2 : 1); ++h)
+                    for (int j = 0; j < 16; ++j) {
+                        const int64_t n = nb + h * 16 + j;
+                        float v = (*cs[r][h])[j] + L.bias[n];
+                        if (relu) v = std::max(v, 0.f);
+                        if (res) v += bf2f(res[(m0 + r) * N + n]);
+                        y[(m0 + r) * N + n] = f2bf(v);
+                    }
+        }
+    }
+}
+
+void layer_norm(int64_t M, int64_t C, const uint16_t *x, uint16_t *y, const float *g, const float *b) {
+    for (int64_t r = 0; r < M; ++r) {
+        const uint16_t *xr = x + r * C;
+        float s = 0.f;
+        for (int64_t c = 0; c < C; ++c) s += bf2f(xr[c]);
+        const float mean = s / float(C);
+        float q = 0.f;
+        for (int64_t c = 0; c < C; ++c) {
+            const float d = bf2f(xr[c]) - mean;
+            q += d * d;
+        }
+        const float rstd = 1.f / std::sqrt(q / float(C) + LN_EPS);
+        for (int64_t c = 0; c < C; ++c) {
+            float o = (bf2f(xr[c]) - mean) * rstd;
+            if (g) o = o * g[c] + b[c];
+            y[r * C + c] = f2bf(o);
+        }
+    }
+}
+
+// Self-attention of P pixels x T steps: qkv (P*T, 1920) -> att (P*T, 640).
+void attention(int64_t P, int64_t T, const uint16_t *qkv, uint16_t *att, std::vector<float> &buf) {
+    const float scale = 1.f / std::sqrt(float(HD));
+    buf.resize(3 * T * HD + T * T + T * HD + T);
+    float *Kt = buf.data();          // [HD][T]
+    float *V = Kt + T * HD;          // [T][HD]
+    float *Q = V + T * HD;           // [T][HD]
+    float *S = Q + T * HD;           // [T][T]
+    float *O = S + T * T;            // [HD]
+    for (int64_t p = 0; p < P; ++p)
+        for (int64_t h = 0; h < NH; ++h) {
+            const uint16_t *base = qkv + p * T * 3 * D + h * HD;
+            for (int64_t t = 0; t < T; ++t)
+                for (int64_t d = 0; d < HD; ++d) {
+                    Q[t * HD + d] = bf2f(base[t * 3 * D + d]);
+                    Kt[d * T + t] = bf2f(base[t * 3 * D + D + d]);
+                    V[t * HD + d] = bf2f(base[t * 3 * D + 2 * D + d]);
+                }
+            for (int64_t t = 0; t < T; ++t) {
+                float *sr = S + t * T;
+                for (int64_t j = 0; j < T; ++j) sr[j] = 0.f;
+                for (int64_t d = 0; d < HD; ++d) {
+                    const float q = Q[t * HD + d];
+                    const float *kr = Kt + d * T;
+                    for (int64_t j = 0; j < T; ++j) sr[j] += q * kr[j];
+                }
+                float mx = -INFINITY;
+                for (int64_t j = 0; j < T; ++j) {
+                    sr[j] = rbf(sr[j] * scale);
+                    mx = std::max(mx, sr[j]);
+                }
+                float z = 0.f;
+                for (int64_t j = 0; j < T; ++j) z += std::exp(sr[j] - mx);
+                const float inv = 1.f / z;
+                for (int64_t j = 0; j < T; ++j) sr[j] = rbf(std::exp(sr[j] - mx) * inv);
+                for (int64_t d = 0; d < HD; ++d) O[d] = 0.f;
+                for (int64_t j = 0; j < T; ++j) {
+                    const float pj = sr[j];
+                    const float *vr = V + j * HD;
+                    for (int64_t d = 0; d < HD; ++d) O[d] += pj * vr[d];
+                }
+                uint16_t *dst = att + (p * T + t) * D + h * HD;
+                for (int64_t d = 0; d < HD; ++d) dst[d] = f2bf(O[d]);
+            }
+        }
+}
+
+struct Backbone {
+    int64_t bands = 0;
+    std::vector<float> w1;  // [640][C] exact bf16 values
+    std::vector<float> b1;
+    Lin emb2, qkv[NL], out[NL], ffn1[NL], ffn2[NL];
+    std::vector<float> n1s[NL], n1b[NL], n2s[NL], n2b[NL];
+    std::vector<float> pool_w;
+    float pool_b = 0.f;
+};
+
+struct Ctx {
+    Backbone bb[2];
+    Lin red1, red2;
+    std::vector<float> rln_s, rln_b;
+    std::vector<uint16_t> pe_table;  // 367 x 640
+    std::string dump_dir;
+    int64_t dump_n = 0;
+    int64_t P = 8;                   // pixels per thread block
+    double wall = 0;
+    uint64_t calls = 0, pixels = 0;
+};
+
+void init_backbone(std::map<std::string, Tensor> &W, Backbone &bb, const std::string &p, int64_t bands) {
+    bb.bands = bands;
+    const Tensor &w1 = W.at(p + ".embedding.0.weight");
+    bb.w1.resize(w1.data.size());
+    for (size_t i = 0; i < w1.data.size(); ++i) bb.w1[i] = rbf(w1.data[i]);
+    bb.b1 = W.at(p + ".embedding.0.bias").data;
+    bb.emb2 = take_linear(W, p + ".embedding.2.weight", p + ".embedding.2.bias");
+    for (int l = 0; l < NL; ++l) {
+        const std::string L = p + ".transformer_encoder.layers." + std::to_string(l);
+        bb.qkv[l] = take_linear(W, L + ".self_attn.in_proj_weight", L + ".self_attn.in_proj_bias");
+        bb.out[l] = take_linear(W, L + ".self_attn.out_proj.weight", L + ".self_attn.out_proj.bias");
+        bb.ffn1[l] = take_linear(W, L + ".linear1.weight", L + ".linear1.bias");
+        bb.ffn2[l] = take_linear(W, L + ".linear2.weight", L + ".linear2.bias");
+        bb.n1s[l] = W.at(L + ".norm1.weight").data;
+        bb.n1b[l] = W.at(L + ".norm1.bias").data;
+        bb.n2s[l] = W.at(L + ".norm2.weight").data;
+        bb.n2b[l] = W.at(L + ".norm2.bias").data;
+    }
+    bb.pool_w = W.at(p + ".attn_pool.query.weight").data;
+    bb.pool_b = W.at(p + ".attn_pool.query.bias").data[0];
+}
+
+struct Scratch {
+    std::vector<uint16_t> y, x, x1, att, qkv, h, pe;
+    std::vector<float> attbuf;
+    std::vector<uint16_t> fused, r1, r2;
+};
+
+// One backbone for P pixels x T steps: in (P, T, C+1) f32 -> fused[:, col0:col0+640] bf16.
+void run_backbone(const Ctx &c, const Backbone &bb, Scratch &s, int64_t P, int64_t T, const float *in,
+                  uint16_t *fused, int64_t col0) {
+    const int64_t M = P * T, C = bb.bands, IN = C + 1;
+    s.y.resize(M * D); s.x.resize(M * D); s.x1.resize(M * D); s.att.resize(M * D);
+    s.qkv.resize(M * 3 * D); s.h.resize(M * FF); s.pe.resize(M * D);
+    // bands -> bf16, emb1 (ReLU), PE rows (tessera_cpu.cpp:387-404)
+    for (int64_t r = 0; r < M; ++r) {
+        const float *row = in + r * IN;
+        float a[16];
+        for (int64_t k = 0; k < C; ++k) a[k] = rbf(row[k]);
+        for (int64_t n = 0; n < D; ++n) {
+            float acc = 0.f;
+            for (int64_t k = 0; k < C; ++k) acc = std::fma(a[k], bb.w1[n * C + k], acc);
+            s.y[r * D + n] = f2bf(std::max(acc + bb.b1[n], 0.f));
+        }
+        const float doy = row[C];
+        const int di = (doy >= 0.f && doy <= 366.f) ? int(doy) : -1;
+        if (di >= 0 && float(di) == doy) {
+            std::memcpy(&s.pe[r * D], c.pe_table.data() + di * D, D * 2);
+        } else {
+            for (int64_t i = 0; i < D / 2; ++i) {
+                const float ang = doy * std::exp(float(2 * i) * -(std::log(10000.0f) / float(D)));
+                s.pe[r * D + 2 * i] = f2bf(std::sin(ang));
+                s.pe[r * D + 2 * i + 1] = f2bf(std::cos(ang));
+            }
+        }
+    }
+    linear(bb.emb2, M, s.y.data(), s.x.data(), false, s.pe.data());
+    for (int l = 0; l < NL; ++l) {
+        linear(bb.qkv[l], M, s.x.data(), s.qkv.data(), false, nullptr);
+        attention(P, T, s.qkv.data(), s.att.data(), s.attbuf);
+        linear(bb.out[l], M, s.att.data(), s.y.data(), false, s.x.data());
+        layer_norm(M, D, s.y.data(), s.x1.data(), bb.n1s[l].data(), bb.n1b[l].data());
+        linear(bb.ffn1[l], M, s.x1.data(), s.h.data(), true, nullptr);
+        linear(bb.ffn2[l], M, s.h.data(), s.y.data(), false, s.x1.data());
+        layer_norm(M, D, s.y.data(), s.x.data(), bb.n2s[l].data(), bb.n2b[l].data());
+    }
+    // attention pooling, f32 (tessera_cpu.cpp:434-455)
+    std::vector<float> sbuf(T), acc(D);
+    for (int64_t p = 0; p < P; ++p) {
+        const uint16_t *xp = s.x.data() + p * T * D;
+        float mx = -INFINITY;
+        for (int64_t t = 0; t < T; ++t) {
+            float d = bb.pool_b;
+            for (int64_t k = 0; k < D; ++k) d += bf2f(xp[t * D + k]) * bb.pool_w[k];
+            sbuf[t] = d;
+            mx = std::max(mx, d);
+        }
+        float z = 0.f;
+        for (int64_t t = 0; t < T; ++t) z += (sbuf[t] = std::exp(sbuf[t] - mx));
+        std::fill(acc.begin(), acc.end(), 0.f);
+        for (int64_t t = 0; t < T; ++t) {
+            const float w = sbuf[t] / z;
+            for (int64_t k = 0; k < D; ++k) acc[k] += w * bf2f(xp[t * D + k]);
+        }
+        for (int64_t k = 0; k < D; ++k) fused[p * 2 * D + col0 + k] = f2bf(acc[k]);
+    }
+}
+
+void dump_call(Ctx &c, const float *s2, int64_t G, int64_t T2, const float *s1, int64_t T1, const float *out) {
+    char name[64];
+    std::snprintf(name, sizeof(name), "/batch_%05ld.bin", (long)c.dump_n++);
+    FILE *f = std::fopen((c.dump_dir + name).c_str(), "wb");
+    if (!f) throw std::runtime_error("cannot write dump " + c.dump_dir + name);
+    const int64_t hdr[3] = {G, T2, T1};
+    std::fwrite(hdr, 8, 3, f);
+    std::fwrite(s2, 4, G * T2 * 11, f);
+    std::fwrite(s1, 4, G * T1 * 3, f);
+    std::fwrite(out, 4, G * OUT, f);
+    std::fclose(f);
+}
+
+}  // namespace
+
+extern "C" {
+
+void *tc_create(const char *weights_path, int /*block_pixels*/) {
+    try {
+        auto W = load_weights(weights_path);
+        auto *c = new Ctx();
+        init_backbone(W, c->bb[0], "s2_backbone", 10);
+        init_backbone(W, c->bb[1], "s1_backbone", 2);
+        c->red1 = take_linear(W, "dim_reducer.0.weight", "dim_reducer.0.bias");
+        c->red2 = take_linear(W, "dim_reducer.4.weight", "dim_reducer.4.bias");
+        c->rln_s = W.at("dim_reducer.1.weight").data;
+        c->rln_b = W.at("dim_reducer.1.bias").data;
+        c->pe_table.resize(367 * D);
+        for (int d = 0; d <= 366; ++d)
+            for (int64_t i = 0; i < D / 2; ++i) {
+                const float a = float(d) * std::exp(float(2 * i) * -(std::log(10000.0f) / float(D)));
+                c->pe_table[d * D + 2 * i] = f2bf(std::sin(a));
+                c->pe_table[d * D + 2 * i + 1] = f2bf(std::cos(a));
+            }
+        if (const char *e = std::getenv("TC_ORACLE_DUMP")) c->dump_dir = e;
+        return c;
+    } catch (const std::exception &e) {
+        std::fprintf(stderr, "tc_create: %s\n", e.what());
+        return nullptr;
+    }
+}
+
+int tc_encode(void *handle, const float *s2, int64_t G, int64_t T2, const float *s1, int64_t T1, float *out) {
+    Ctx &c = *static_cast<Ctx *>(handle);
+    const double t0 = omp_get_wtime();
+    try {
+        if (G <= 0) return 0;
+        if (T2 < 1 || T1 < 1) throw std::runtime_error("T2 and T1 must be >= 1");
+        const int64_t P = c.P, nblk = (G + P - 1) / P;
+        int err = 0;
+#pragma omp parallel
+        {
+            Scratch s;
+            std::vector<float> pad2, pad1;
+#pragma omp for schedule(dynamic, 1)
+            for (int64_t bi = 0; bi < nblk; ++bi) {
+                if (err) continue;
+                try {
+                    const int64_t p0 = bi * P, n = std::min(P, G - p0);
+                    const float *in2 = s2 + p0 * T2 * 11, *in1 = s1 + p0 * T1 * 3;
+                    s.fused.assign(n * 2 * D, 0);
+                    run_backbone(c, c.bb[0], s, n, T2, in2, s.fused.data(), 0);
+                    run_backbone(c, c.bb[1], s, n, T1, in1, s.fused.data(), D);
+                    s.r1.resize(n * RED);
+                    s.r2.resize(n * OUT);
+                    linear(c.red1, n, s.fused.data(), s.r1.data(), false, nullptr);
+                    layer_norm(n, RED, s.r1.data(), s.r1.data(), c.rln_s.data(), c.rln_b.data());
+                    for (auto &v : s.r1)
+                        if (v & 0x8000u) v = 0;  // relu on bf16 (tessera_cpu.cpp:570-571)
+                    linear(c.red2, n, s.r1.data(), s.r2.data(), false, nullptr);
+                    layer_norm(n, OUT, s.r2.data(), s.r2.data(), nullptr, nullptr);
+                    for (int64_t i = 0; i < n * OUT; ++i) out[p0 * OUT + i] = bf2f(s.r2[i]);
+                } catch (const std::exception &ex) {
+                    std::fprintf(stderr, "tc_encode block %ld: %s\n", (long)bi, ex.what());
+#pragma omp atomic write
+                    err = 1;
+                }
+            }
+        }
+        if (err) return -1;
+        if (!c.dump_dir.empty()) dump_call(c, s2, G, T2, s1, T1, out);
+        c.wall += omp_get_wtime() - t0;
+        ++c.calls;
+        c.pixels += G;
+        return 0;
+    } catch (const std::exception &e) {
+        std::fprintf(stderr, "tc_encode: %s\n", e.what());
+        return -1;
+    }
+}
+
+void tc_profile_dump(void *handle) {
+    Ctx &c = *static_cast<Ctx *>(handle);
+    std::printf("TCPROF oracle (CPU restatement, not oneDNN) calls=%lu px=%lu threads=%d tc_encode wall %.2f s\n",
+                (unsigned long)c.calls, (unsigned long)c.pixels, omp_get_max_threads(), c.wall);
+    std::fflush(stdout);
+}
+
+void tc_destroy(void *handle) { delete static_cast<Ctx *>(handle); }
+
+}  // extern "C"

@@ -1,0 +1,325 @@
+// Dense layers of the pixel student on the sm_100a tensor cores.
+//
+//   out[M, N] (bf16) = round_bf16( [relu]( A[M, K] . W[N, K]^T + bias[N] ) [+ residual[M, N]] )
+//
+// A is a token-major activation matrix, W a torch-layout (out x in) weight
+// matrix; both are bf16 and K-contiguous. This is the rounding contract of the
+// reference's oneDNN matmul with bias + [relu] + [binary add] post-ops
+// (tessera_cpu.cpp:215-243): f32 accumulation, f32 bias, residual added in f32,
+// one round-to-nearest-even to bf16 at the end.
+//
+// Kernel shape: persistent, one CTA per SM, warp-specialised.
+//   warp 0      TMA producer: A and W tiles (128-byte swizzle) into a ring of
+//               shared-memory stages, completion tracked by mbarriers.
+//   warp 1      TMEM allocator and MMA issuer: one elected thread issues
+//               tcgen05.mma (M=128, N=BN, K=16) into a double-buffered f32
+//               accumulator in tensor memory and commits stage/tile barriers.
+//   warps 2-5   epilogue: tcgen05.ld of the accumulator (one TMEM lane
+//               quadrant per warp, one output row per thread), bias, ReLU,
+//               residual, bf16 rounding, 16-byte stores.
+// The double-buffered accumulator lets the epilogue of tile i overlap the
+// main loop of tile i+1.
+#include <cstdio>
+#include <mutex>
+#include <stdexcept>
+#include <string>
+
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+#include "gemm_sm100.h"
+
+namespace tcb {
+
+constexpr int BM = 128;           // UMMA M (cta_group::1)
+constexpr int BK = 64;            // one 128-byte swizzle atom of bf16 along K
+constexpr int UMMA_K = 16;        // K per tcgen05.mma for 16-bit inputs
+constexpr int GEMM_THREADS = 192; // 6 warps
+constexpr int SMEM_BUDGET = 225 * 1024;
+
+template <int BN> struct GemmCfg {
+    static constexpr int A_BYTES = BM * BK * 2;
+    static constexpr int B_BYTES = BN * BK * 2;
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int STAGES_RAW = (SMEM_BUDGET - 2048) / STAGE_BYTES;
+    static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
+    static constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * STAGE_BYTES + 256 /*barriers*/;
+    static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N for M=128 must be a multiple of 16 in [16,256]");
+    static_assert(B_BYTES % 1024 == 0, "B stage must keep 1024-byte alignment for the 128B swizzle");
+    static_assert(STAGES >= 2, "need at least two pipeline stages");
+};
+
+__device__ __forceinline__ float pe_value(float doy, int n, const bf16 *__restrict__ table,
+                                          const float *__restrict__ div, bool tab, int di) {
+    if (tab) return __bfloat162float(table[di * D + n]);
+    const float a = doy * div[n >> 1];
+    return bf16_round((n & 1) ? cosf(a) : sinf(a));
+}
+
+template <int BN>
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
+    k_gemm_bf16(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs p) {
+    using Cfg = GemmCfg<BN>;
+    constexpr int S = Cfg::STAGES;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *sA = smem;
+    uint8_t *sB = smem + S * Cfg::A_BYTES;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + S * Cfg::STAGE_BYTES);
+    uint64_t *full = bars, *empty = bars + S, *tfull = bars + 2 * S, *tempty = bars + 2 * S + 2;
+    uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 2 * S + 4);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int num_n = p.N / BN;
+    const int num_m = (p.M + BM - 1) / BM;
+    const int ntiles = num_m * num_n;
+    const int nk = p.K / BK;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < S; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 1); }
+        for (int i = 0; i < 2; ++i) { mbar_init(&tfull[i], 1); mbar_init(&tempty[i], 4); }
+        *abort_flag = 0;
+        fence_mbar_init();
+        prefetch_tensormap(&tmA);
+        prefetch_tensormap(&tmB);
+    }
+    if (warp == 1) { tmem_alloc(tmem_holder, 512); tmem_relinquish(); }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_holder;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int s = 0;
+            uint32_t ph = 0;
+            for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
+                const int m0 = (t / num_n) * BM, n0 = (t % num_n) * BN;
+                bool ok = true;
+                for (int kb = 0; kb < nk; ++kb) {
+                    if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, p.status, ERR_WAIT_SMEM_EMPTY)) { ok = false; break; }
+                    mbar_arrive_expect_tx(&full[s], Cfg::STAGE_BYTES);
+                    tma_load_2d(sA + s * Cfg::A_BYTES, &tmA, kb * BK, m0, &full[s]);
+                    tma_load_2d(sB + s * Cfg::B_BYTES, &tmB, kb * BK, n0, &full[s]);
+                    if (++s == S) { s = 0; ph ^= 1; }
+                }
+                if (!ok) break;
+            }
+            // Producer tail: wait until every stage's last fill has been released by
+            // its MMA commit, so no tensor-core arrival is still in flight at exit.
+            for (int i = 0; i < S; ++i) {
+                if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, p.status, ERR_WAIT_SMEM_EMPTY)) break;
+                if (++s == S) { s = 0; ph ^= 1; }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = umma_idesc_bf16(BM, BN);
+            int s = 0;
+            uint32_t ph = 0;
+            int tl = 0;
+            for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++tl) {
+                const int buf = tl & 1;
+                const uint32_t use = (uint32_t)(tl >> 1);
+                if (!mbar_wait(&tempty[buf], (use & 1) ^ 1, abort_flag, p.status, ERR_WAIT_TMEM_EMPTY)) break;
+                tc_fence_after();
+                const uint32_t d = tmem_base + (uint32_t)(buf * BN);
+                bool ok = true;
+                for (int kb = 0; kb < nk; ++kb) {
+                    if (!mbar_wait(&full[s], ph, abort_flag, p.status, ERR_WAIT_TMA_FULL)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint64_t adesc = umma_desc_sw128(smem_u32(sA + s * Cfg::A_BYTES));
+                    const uint64_t bdesc = umma_desc_sw128(smem_u32(sB + s * Cfg::B_BYTES));
+#pragma unroll
+                    for (int k = 0; k < BK / UMMA_K; ++k) {
+                        // +32 bytes along K inside the swizzle atom = +2 in the >>4 address field
+                        umma_bf16(d, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), idesc,
+                                  (kb | k) != 0 ? 1u : 0u);
+                    }
+                    umma_commit(&empty[s]);
+                    if (++s == S) { s = 0; ph ^= 1; }
+                }
+                if (!ok) break;
+                umma_commit(&tfull[buf]);
+            }
+        }
+    } else {
+        // epilogue warps 2..5: TMEM lane quadrant = warp % 4
+        const int quad = warp & 3;
+        const int row_in_tile = quad * 32 + lane;
+        int tl = 0;
+        for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++tl) {
+            const int m0 = (t / num_n) * BM, n0 = (t % num_n) * BN;
+            const int buf = tl & 1;
+            const uint32_t use = (uint32_t)(tl >> 1);
+            if (!mbar_wait(&tfull[buf], use & 1, abort_flag, p.status, ERR_WAIT_TMEM_FULL)) break;
+            tc_fence_after();
+            const int row = m0 + row_in_tile;
+            const bool live = row < p.M;
+            // residual source for this row
+            const bf16 *res_row = nullptr;
+            bool pe_tab = false;
+            int pe_di = 0;
+            float pe_doy = 0.f;
+            if (live) {
+                if (p.res) res_row = p.res + (size_t)row * p.ldr;
+                if (p.pe_doy) {
+                    pe_doy = p.pe_doy[(size_t)row * p.pe_stride];
+                    if (pe_doy >= 0.f && pe_doy <= 366.f && floorf(pe_doy) == pe_doy) {
+                        pe_tab = true;
+                        pe_di = (int)pe_doy;
+                    }
+                }
+            }
+            bf16 *out_row = p.out + (size_t)row * p.ldo;
+            const uint32_t tbase = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * BN);
+#pragma unroll 1
+            for (int c = 0; c < BN; c += 16) {
+                uint32_t r[16];
+                tmem_ld16(tbase + (uint32_t)c, r);
+                tmem_ld_wait();
+                if (live) {
+                    const int n = n0 + c;
+                    float v[16];
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
+                    if (p.bias) {
+                        const float4 *b4 = reinterpret_cast<const float4 *>(p.bias + n);
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            const float4 b = __ldg(b4 + j);
+                            v[4 * j] += b.x; v[4 * j + 1] += b.y; v[4 * j + 2] += b.z; v[4 * j + 3] += b.w;
+                        }
+                    }
+                    if (p.relu) {
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) v[j] = fmaxf(v[j], 0.f);
+                    }
+                    if (res_row) {
+                        const uint4 *r4 = reinterpret_cast<const uint4 *>(res_row + n);
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) {
+                            const uint4 q = r4[h];
+                            const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+                            for (int j = 0; j < 4; ++j) {
+                                v[8 * h + 2 * j] += bf16lo(w[j]);
+                                v[8 * h + 2 * j + 1] += bf16hi(w[j]);
+                            }
+                        }
+                    } else if (p.pe_doy) {
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) v[j] += pe_value(pe_doy, n + j, p.pe_table, p.pe_div, pe_tab, pe_di);
+                    }
+                    uint4 o[2];
+                    o[0] = make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]),
+                                      pack_bf16x2(v[6], v[7]));
+                    o[1] = make_uint4(pack_bf16x2(v[8], v[9]), pack_bf16x2(v[10], v[11]), pack_bf16x2(v[12], v[13]),
+                                      pack_bf16x2(v[14], v[15]));
+                    uint4 *dst = reinterpret_cast<uint4 *>(out_row + n);
+                    dst[0] = o[0];
+                    dst[1] = o[1];
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[buf]);
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc(tmem_base, 512);
+}
+
+// ------------------------------------------------------------------ host side
+
+static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    });
+    return fn;
+}
+
+// 2-D bf16 tensor map over a row-major [rows, cols] matrix (cols contiguous),
+// box = [box_rows, 64 columns], 128-byte swizzle. Rows past `rows` read as zero.
+static void make_tmap(CUtensorMap *tm, const void *ptr, uint64_t rows, uint64_t cols, uint64_t ld_elems,
+                      uint32_t box_rows) {
+    auto enc = get_encode_fn();
+    if (!enc) throw std::runtime_error("cuTensorMapEncodeTiled unavailable");
+    if (reinterpret_cast<uintptr_t>(ptr) % 16) throw std::runtime_error("TMA base address not 16-byte aligned");
+    if ((ld_elems * 2) % 16) throw std::runtime_error("TMA row pitch not a multiple of 16 bytes");
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {ld_elems * 2};
+    cuuint32_t box[2] = {(cuuint32_t)BK, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(ptr), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
+}
+
+static int num_sms() {
+    static int n = 0;
+    if (!n) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        if (n <= 0) n = 148;
+    }
+    return n;
+}
+
+template <int BN> static void launch_bn(const GemmArgs &p, const bf16 *A, int lda, const bf16 *W, cudaStream_t st,
+                                        int max_ctas) {
+    using Cfg = GemmCfg<BN>;
+    static bool attr_set[64] = {};  // per device
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!attr_set[dev & 63]) {
+        cudaError_t e = cudaFuncSetAttribute(k_gemm_bf16<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
+        if (e != cudaSuccess) throw std::runtime_error(std::string("gemm smem attribute: ") + cudaGetErrorString(e));
+        attr_set[dev & 63] = true;
+    }
+    CUtensorMap ta, tb;
+    make_tmap(&ta, A, (uint64_t)p.M, (uint64_t)p.K, (uint64_t)lda, BM);
+    make_tmap(&tb, W, (uint64_t)p.N, (uint64_t)p.K, (uint64_t)p.K, BN);
+    const int ntiles = ((p.M + BM - 1) / BM) * (p.N / BN);
+    int grid = std::min(ntiles, num_sms());
+    if (max_ctas > 0) grid = std::min(grid, max_ctas);
+    if (grid < 1) grid = 1;
+    k_gemm_bf16<BN><<<grid, GEMM_THREADS, Cfg::SMEM_BYTES, st>>>(ta, tb, p);
+}
+
+int gemm_pick_bn(int N) {
+    if (N % 256 == 0) return 256;
+    if (N % 240 == 0) return 240;
+    if (N % 160 == 0) return 160;
+    if (N % 128 == 0) return 128;
+    return 0;
+}
+
+void launch_gemm(const GemmArgs &p, const bf16 *A, int lda, const bf16 *W, cudaStream_t st, int bn, int max_ctas) {
+    if (p.M <= 0) return;
+    if (p.K % BK) throw std::runtime_error("gemm: K must be a multiple of 64");
+    if (bn == 0) bn = gemm_pick_bn(p.N);
+    if (bn == 0 || p.N % bn) throw std::runtime_error("gemm: unsupported N " + std::to_string(p.N));
+    if (p.ldo % 8 || (p.res && p.ldr % 8)) throw std::runtime_error("gemm: output/residual pitch must be 16-byte aligned");
+    switch (bn) {
+    case 256: launch_bn<256>(p, A, lda, W, st, max_ctas); break;
+    case 240: launch_bn<240>(p, A, lda, W, st, max_ctas); break;
+    case 160: launch_bn<160>(p, A, lda, W, st, max_ctas); break;
+    case 128: launch_bn<128>(p, A, lda, W, st, max_ctas); break;
+    default: throw std::runtime_error("gemm: unsupported tile width " + std::to_string(bn));
+    }
+}
+
+}  // namespace tcb

@@ -1,0 +1,37 @@
+// Host interface of the tcgen05 GEMM (gemm_sm100.cu).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+namespace tcb {
+
+// out = round_bf16([relu](A . W^T + bias) [+ residual]) for row-major bf16 A [M, K]
+// and W [N, K]. Exactly one residual source may be set: `res` (a bf16 matrix
+// with pitch ldr) or `pe_doy` (per-row day of year; the residual row is the
+// bf16 sinusoid of that day, from `pe_table` when the day is an integer in
+// [0, 366], else computed from `pe_div`).
+struct GemmArgs {
+    int M = 0, N = 0, K = 0;
+    const float *bias = nullptr;
+    int relu = 0;
+    const __nv_bfloat16 *res = nullptr;
+    int ldr = 0;
+    const float *pe_doy = nullptr;
+    int pe_stride = 1;
+    const __nv_bfloat16 *pe_table = nullptr;
+    const float *pe_div = nullptr;
+    __nv_bfloat16 *out = nullptr;
+    int ldo = 0;
+    int *status = nullptr;  // device status word (0 = ok)
+};
+
+// Tile width BN used for a given N (0 = unsupported).
+int gemm_pick_bn(int N);
+
+// Enqueue one GEMM on `st`. bn = 0 picks the tile width; max_ctas > 0 caps the
+// persistent grid. Throws std::runtime_error on unsupported shapes.
+void launch_gemm(const GemmArgs &p, const __nv_bfloat16 *A, int lda, const __nv_bfloat16 *W, cudaStream_t st,
+                 int bn = 0, int max_ctas = 0);
+
+}  // namespace tcb

@@ -1,0 +1,565 @@
+// Warp-level kernels of the pixel-student forward pass: input preparation
+// (valid counts, pad pattern, gather + z-score), the K=10/2 embedding layer,
+// per-pixel self-attention, LayerNorm, attention pooling and the head's
+// LayerNorms with the int8 quantisation.
+//
+// Rounding follows the reference CPU back end (tessera_cpu.cpp) and driver
+// (tessera_encode.cpp): inputs z-scored in f32 with IEEE division, bf16 RNE at
+// every layer boundary, f32 statistics and softmax.
+#include <cmath>
+#include <stdexcept>
+#include <string>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace tcb {
+
+// ------------------------------------------------------------------ constants
+// Standardisation constants of tessera_v2_student (tessera_encode.cpp:60-67).
+__constant__ float c_s2_mean[10] = {1633.0042f, 1341.1090f, 1539.5536f, 3054.8269f, 3117.4658f,
+                                    2004.1648f, 2694.7275f, 2945.1504f, 2266.6079f, 1657.3094f};
+__constant__ float c_s2_std[10] = {1999.4603f, 2014.7549f, 1929.2201f, 1754.2493f, 1649.9807f,
+                                   1936.8988f, 1748.6041f, 1708.6991f, 1207.5250f, 1108.6046f};
+__constant__ float c_s1a_mean[2] = {5909.3921f, 3405.0322f};
+__constant__ float c_s1a_std[2] = {1507.1750f, 1531.2615f};
+__constant__ float c_s1d_mean[2] = {5816.1382f, 3277.7576f};
+__constant__ float c_s1d_std[2] = {1554.6475f, 1546.4733f};
+constexpr float Z_EPS = 1e-9f;
+
+__device__ __forceinline__ int64_t seg_at(const Segs &s, int64_t i) {
+    return s.off ? s.off[i] - s.base : i * s.uniform_T;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+static void check_launch(const char *what) {
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+// ------------------------------------------------------------------ prep
+// Valid counts: S2 mask != 0; S1 either band != 0 (tessera_encode.cpp:249-255).
+__global__ void k_count(TileDev t, int64_t p0, int64_t np, int32_t *n2, int32_t *n1) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= np) return;
+    const int64_t p = p0 + i, N = t.N;
+    int c2 = 0, c1 = 0;
+    for (int64_t s = 0; s < t.T2; ++s) c2 += t.masks[s * N + p] != 0;
+    const uint32_t *a = reinterpret_cast<const uint32_t *>(t.asc);
+    const uint32_t *d = reinterpret_cast<const uint32_t *>(t.desc);
+    for (int64_t s = 0; s < t.Ta; ++s) c1 += a[s * N + p] != 0u;
+    for (int64_t s = 0; s < t.Td; ++s) c1 += d[s * N + p] != 0u;
+    n2[i] = c2;
+    n1[i] = c1;
+}
+
+// _pad_pattern(n, B)[k] for n > 0 (tessera_encode.cpp:154-180): numpy
+// linspace floor when n >= B, middle of each array_split group when the
+// shortfall is at most n, otherwise modulo fill.
+__device__ __forceinline__ int64_t pad_index(int64_t n, int64_t B, int64_t k) {
+    if (n >= B) {
+        if (B == 1) return 0;
+        if (k == B - 1) return n - 1;
+        const double delta = double(n - 1), div = double(B - 1), step = delta / div;
+        const double y = step == 0 ? (double(k) / div) * delta : double(k) * step;
+        return (int64_t)floor(y);
+    }
+    if (k < n) return k;
+    const int64_t g = k - n, remain = B - n;
+    if (remain <= n) {
+        const int64_t q = n / remain, r = n % remain;
+        const int64_t start = g * q + (g < r ? g : r);
+        const int64_t len = q + (g < r ? 1 : 0);
+        return start + len / 2;
+    }
+    return g % n;
+}
+
+// One warp per pixel: ordered valid-step list by ballot, then B padded steps.
+template <int MOD>
+__global__ void __launch_bounds__(128) k_gather(TileDev t, int64_t p0, int64_t np, const int32_t *bins, Segs segs,
+                                                float *rec) {
+    constexpr int C = MOD == 0 ? 10 : 2;
+    __shared__ uint16_t lists[4][MAX_STEPS];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t i = (int64_t)blockIdx.x * 4 + warp;
+    if (i >= np) return;
+    const int64_t B = bins[i];
+    if (B <= 0) return;
+    const int64_t p = p0 + i, N = t.N;
+    const int64_t Tsteps = MOD == 0 ? t.T2 : t.Ta + t.Td;
+    uint16_t *list = lists[warp];
+    const uint32_t *a32 = reinterpret_cast<const uint32_t *>(t.asc);
+    const uint32_t *d32 = reinterpret_cast<const uint32_t *>(t.desc);
+    int nv = 0;
+    for (int64_t base = 0; base < Tsteps; base += 32) {
+        const int64_t s = base + lane;
+        bool v = false;
+        if (s < Tsteps) {
+            if (MOD == 0) v = t.masks[s * N + p] != 0;
+            else v = (s < t.Ta ? a32[s * N + p] : d32[(s - t.Ta) * N + p]) != 0u;
+        }
+        const uint32_t m = __ballot_sync(0xffffffffu, v);
+        if (v) list[nv + __popc(m & ((1u << lane) - 1u))] = (uint16_t)s;
+        nv += __popc(m);
+    }
+    __syncwarp();
+    float *out = rec + seg_at(segs, i) * (C + 1);
+    for (int64_t k = lane; k < B; k += 32) {
+        float *row = out + k * (C + 1);
+        if (nv == 0) {  // empty modality: one all-zero row (tessera_encode.cpp:275,279-280)
+#pragma unroll
+            for (int c = 0; c <= C; ++c) row[c] = 0.f;
+            continue;
+        }
+        const int64_t s = list[pad_index(nv, B, k)];
+        if (MOD == 0) {
+            const uint16_t *src = t.bands + (s * N + p) * 10;
+#pragma unroll
+            for (int c = 0; c < 10; ++c) row[c] = (float(src[c]) - c_s2_mean[c]) / (c_s2_std[c] + Z_EPS);
+            row[10] = float(t.doys[s]);
+        } else if (s < t.Ta) {
+            const int16_t *v = t.asc + (s * N + p) * 2;
+#pragma unroll
+            for (int c = 0; c < 2; ++c) row[c] = (float(v[c]) - c_s1a_mean[c]) / (c_s1a_std[c] + Z_EPS);
+            row[2] = float(t.asc_doy[s]);
+        } else {
+            const int16_t *v = t.desc + ((s - t.Ta) * N + p) * 2;
+#pragma unroll
+            for (int c = 0; c < 2; ++c) row[c] = (float(v[c]) - c_s1d_mean[c]) / (c_s1d_std[c] + Z_EPS);
+            row[2] = float(t.desc_doy[s - t.Ta]);
+        }
+    }
+}
+
+// ------------------------------------------------------------------ emb1
+// Warp per token; lane computes columns lane*4 + 128*j (j < 5).
+template <int C>
+__global__ void __launch_bounds__(256) k_emb1(const float *__restrict__ rec, int64_t M, const float *__restrict__ w1t,
+                                              const float *__restrict__ b1, bf16 *__restrict__ y) {
+    __shared__ float ws[C * D];
+    __shared__ float bs[D];
+    for (int i = threadIdx.x; i < C * D; i += blockDim.x) ws[i] = w1t[i];
+    for (int i = threadIdx.x; i < D; i += blockDim.x) bs[i] = b1[i];
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    for (int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp; r < M; r += nwarps) {
+        float a[C];
+#pragma unroll
+        for (int k = 0; k < C; ++k) a[k] = bf16_round(__ldg(rec + r * (C + 1) + k));
+        bf16 *yr = y + r * D;
+#pragma unroll
+        for (int j = 0; j < 5; ++j) {
+            const int n = j * 128 + lane * 4;
+            float acc[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                float s = 0.f;
+#pragma unroll
+                for (int k = 0; k < C; ++k) s = fmaf(a[k], ws[k * D + n + q], s);
+                acc[q] = fmaxf(s + bs[n + q], 0.f);
+            }
+            *reinterpret_cast<uint2 *>(yr + n) = make_uint2(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]));
+        }
+    }
+}
+
+// ------------------------------------------------------------------ attention
+constexpr int ATT_LD = HD + 8;  // smem row pitch of K/V tiles (336 B): conflict-free ldmatrix
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// One CTA per (pixel, head). K and V of the head are staged in shared memory;
+// each warp owns 16 query rows: S = bf16(scale * Q K^T) over all keys, softmax
+// in f32 over the T valid keys, P rounded to bf16, O = bf16(P V)
+// (tessera_cpu.cpp:333-343: matmul + linear post-op, softmax_accurate, matmul).
+__global__ void __launch_bounds__(256) k_attention(const bf16 *__restrict__ qkv, Segs segs, bf16 *__restrict__ att,
+                                                   float scale) {
+    extern __shared__ __align__(16) uint8_t att_smem[];
+    const int64_t i = blockIdx.x;
+    const int h = blockIdx.y;
+    const int64_t t0 = seg_at(segs, i);
+    const int T = (int)(seg_at(segs, i + 1) - t0);
+    if (T <= 0) return;
+    const int Tpad = (T + 15) & ~15;
+    bf16 *Ks = reinterpret_cast<bf16 *>(att_smem);
+    bf16 *Vs = Ks + Tpad * ATT_LD;
+    const uint4 *qkv4 = reinterpret_cast<const uint4 *>(qkv);
+    for (int idx = threadIdx.x; idx < Tpad * (HD / 8); idx += blockDim.x) {
+        const int r = idx / (HD / 8), c = idx % (HD / 8);
+        uint4 kk = make_uint4(0, 0, 0, 0), vv = kk;
+        if (r < T) {
+            const int64_t rb = (t0 + r) * (3 * D / 8);
+            kk = qkv4[rb + D / 8 + h * (HD / 8) + c];
+            vv = qkv4[rb + 2 * D / 8 + h * (HD / 8) + c];
+        }
+        *reinterpret_cast<uint4 *>(Ks + r * ATT_LD + c * 8) = kk;
+        *reinterpret_cast<uint4 *>(Vs + r * ATT_LD + c * 8) = vv;
+    }
+    __syncthreads();
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, tq = lane & 3;
+    const int nwarps = blockDim.x >> 5;
+    const int nrb = Tpad / 16, nnt = Tpad / 8;
+    const uint32_t ks_base = smem_u32(Ks), vs_base = smem_u32(Vs);
+    for (int rb = warp; rb < nrb; rb += nwarps) {
+        const int r0 = rb * 16 + g, r1 = r0 + 8;
+        uint32_t qa[HD / 16][4];
+        {
+            const uint32_t *q0 = r0 < T ? reinterpret_cast<const uint32_t *>(qkv + (t0 + r0) * (3 * D) + h * HD) : nullptr;
+            const uint32_t *q1 = r1 < T ? reinterpret_cast<const uint32_t *>(qkv + (t0 + r1) * (3 * D) + h * HD) : nullptr;
+#pragma unroll
+            for (int ks = 0; ks < HD / 16; ++ks) {
+                qa[ks][0] = q0 ? __ldg(q0 + ks * 8 + tq) : 0u;
+                qa[ks][1] = q1 ? __ldg(q1 + ks * 8 + tq) : 0u;
+                qa[ks][2] = q0 ? __ldg(q0 + ks * 8 + 4 + tq) : 0u;
+                qa[ks][3] = q1 ? __ldg(q1 + ks * 8 + 4 + tq) : 0u;
+            }
+        }
+        // S tiles, packed bf16: sp[nt][0] row r0 cols (nt*8 + 2tq, +1), sp[nt][1] row r1.
+        uint32_t sp[32][2];
+#pragma unroll
+        for (int nt = 0; nt < 32; ++nt) {
+            if (nt < nnt) {
+                float c[4] = {0.f, 0.f, 0.f, 0.f};
+                const uint32_t addr = ks_base + (uint32_t)(((nt * 8 + (lane & 7)) * ATT_LD + (lane >> 3) * 8) * 2);
+#pragma unroll
+                for (int ks = 0; ks < HD / 16; ks += 2) {
+                    uint32_t b0, b1, b2, b3;
+                    ldsm_x4(addr + ks * 32, b0, b1, b2, b3);
+                    mma_bf16_16816(c, qa[ks], b0, b1);
+                    mma_bf16_16816(c, qa[ks + 1], b2, b3);
+                }
+                const int col = nt * 8 + 2 * tq;
+                const float ninf = -INFINITY;
+                const float s0 = col < T ? c[0] * scale : ninf, s1 = col + 1 < T ? c[1] * scale : ninf;
+                const float s2 = col < T ? c[2] * scale : ninf, s3 = col + 1 < T ? c[3] * scale : ninf;
+                sp[nt][0] = pack_bf16x2(s0, s1);
+                sp[nt][1] = pack_bf16x2(s2, s3);
+            }
+        }
+        // softmax over keys: rows r0 (sp[.][0]) and r1 (sp[.][1]); a row lives in one lane quad
+        float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+        for (int nt = 0; nt < 32; ++nt)
+            if (nt < nnt) {
+                mx0 = fmaxf(mx0, fmaxf(bf16lo(sp[nt][0]), bf16hi(sp[nt][0])));
+                mx1 = fmaxf(mx1, fmaxf(bf16lo(sp[nt][1]), bf16hi(sp[nt][1])));
+            }
+#pragma unroll
+        for (int o = 1; o <= 2; o <<= 1) {
+            mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
+            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
+        }
+        float z0 = 0.f, z1 = 0.f;
+#pragma unroll
+        for (int nt = 0; nt < 32; ++nt)
+            if (nt < nnt) {
+                z0 += expf(bf16lo(sp[nt][0]) - mx0) + expf(bf16hi(sp[nt][0]) - mx0);
+                z1 += expf(bf16lo(sp[nt][1]) - mx1) + expf(bf16hi(sp[nt][1]) - mx1);
+            }
+#pragma unroll
+        for (int o = 1; o <= 2; o <<= 1) {
+            z0 += __shfl_xor_sync(0xffffffffu, z0, o);
+            z1 += __shfl_xor_sync(0xffffffffu, z1, o);
+        }
+        const float inv0 = 1.f / z0, inv1 = 1.f / z1;
+#pragma unroll
+        for (int nt = 0; nt < 32; ++nt)
+            if (nt < nnt) {
+                sp[nt][0] = pack_bf16x2(expf(bf16lo(sp[nt][0]) - mx0) * inv0, expf(bf16hi(sp[nt][0]) - mx0) * inv0);
+                sp[nt][1] = pack_bf16x2(expf(bf16lo(sp[nt][1]) - mx1) * inv1, expf(bf16hi(sp[nt][1]) - mx1) * inv1);
+            }
+        // O = P V
+        float o[HD / 8][4];
+#pragma unroll
+        for (int dn = 0; dn < HD / 8; ++dn) o[dn][0] = o[dn][1] = o[dn][2] = o[dn][3] = 0.f;
+#pragma unroll
+        for (int kt = 0; kt < 16; ++kt) {
+            if (kt < nrb) {
+                const uint32_t a[4] = {sp[2 * kt][0], sp[2 * kt][1], sp[2 * kt + 1][0], sp[2 * kt + 1][1]};
+                const int vrow = kt * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+                const uint32_t addr = vs_base + (uint32_t)((vrow * ATT_LD + (lane >> 4) * 8) * 2);
+#pragma unroll
+                for (int dn2 = 0; dn2 < HD / 16; ++dn2) {
+                    uint32_t b0, b1, b2, b3;
+                    ldsm_x4_t(addr + dn2 * 32, b0, b1, b2, b3);
+                    mma_bf16_16816(o[2 * dn2], a, b0, b1);
+                    mma_bf16_16816(o[2 * dn2 + 1], a, b2, b3);
+                }
+            }
+        }
+        if (r0 < T) {
+            uint32_t *dst = reinterpret_cast<uint32_t *>(att + (t0 + r0) * D + h * HD);
+#pragma unroll
+            for (int dn = 0; dn < HD / 8; ++dn) dst[dn * 4 + tq] = pack_bf16x2(o[dn][0], o[dn][1]);
+        }
+        if (r1 < T) {
+            uint32_t *dst = reinterpret_cast<uint32_t *>(att + (t0 + r1) * D + h * HD);
+#pragma unroll
+            for (int dn = 0; dn < HD / 8; ++dn) dst[dn * 4 + tq] = pack_bf16x2(o[dn][2], o[dn][3]);
+        }
+    }
+}
+
+// ------------------------------------------------------------------ LayerNorm
+// Warp per row of 640: lane holds columns lane*4 + 128*j. Two-pass f32 stats.
+__global__ void __launch_bounds__(256) k_layernorm640(const bf16 *__restrict__ x, int64_t M, const float *__restrict__ g,
+                                                      const float *__restrict__ b, bf16 *__restrict__ y) {
+    const int64_t r = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (r >= M) return;
+    const bf16 *xr = x + r * D;
+    float v[20];
+#pragma unroll
+    for (int j = 0; j < 5; ++j) {
+        const uint2 q = *reinterpret_cast<const uint2 *>(xr + j * 128 + lane * 4);
+        v[4 * j] = bf16lo(q.x); v[4 * j + 1] = bf16hi(q.x); v[4 * j + 2] = bf16lo(q.y); v[4 * j + 3] = bf16hi(q.y);
+    }
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < 20; ++j) s += v[j];
+    const float mean = warp_sum(s) / (float)D;
+    float q = 0.f;
+#pragma unroll
+    for (int j = 0; j < 20; ++j) { const float d = v[j] - mean; q += d * d; }
+    const float rstd = 1.f / sqrtf(warp_sum(q) / (float)D + LN_EPS);
+    bf16 *yr = y + r * D;
+#pragma unroll
+    for (int j = 0; j < 5; ++j) {
+        const int c = j * 128 + lane * 4;
+        float o[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            o[k] = (v[4 * j + k] - mean) * rstd;
+            if (g) o[k] = o[k] * g[c + k] + b[c + k];
+        }
+        *reinterpret_cast<uint2 *>(yr + c) = make_uint2(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]));
+    }
+}
+
+// ------------------------------------------------------------------ pooling
+// One CTA (160 threads) per pixel: warp-per-step logits, softmax in warp 0,
+// then each thread accumulates 4 columns over the steps.
+__global__ void __launch_bounds__(160) k_pool(const bf16 *__restrict__ x, Segs segs, const float *__restrict__ q,
+                                              float qb, bf16 *__restrict__ fused, int col0) {
+    __shared__ float w[256];
+    __shared__ float zs;
+    const int64_t i = blockIdx.x;
+    const int64_t t0 = seg_at(segs, i);
+    const int T = (int)(seg_at(segs, i + 1) - t0);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    bf16 *fo = fused + i * (2 * D) + col0;
+    if (T <= 0) {  // pixel with no observation at all: zero row (never reaches the output)
+        *reinterpret_cast<uint2 *>(fo + threadIdx.x * 4) = make_uint2(0u, 0u);
+        return;
+    }
+    const bf16 *xp = x + t0 * D;
+    for (int t = warp; t < T; t += 5) {
+        float d = 0.f;
+#pragma unroll
+        for (int j = 0; j < 5; ++j) {
+            const int c = j * 128 + lane * 4;
+            const uint2 v = *reinterpret_cast<const uint2 *>(xp + (int64_t)t * D + c);
+            d += bf16lo(v.x) * q[c] + bf16hi(v.x) * q[c + 1] + bf16lo(v.y) * q[c + 2] + bf16hi(v.y) * q[c + 3];
+        }
+        d = warp_sum(d);
+        if (lane == 0) w[t] = d + qb;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        float mx = -INFINITY;
+        for (int t = lane; t < T; t += 32) mx = fmaxf(mx, w[t]);
+        mx = warp_max(mx);
+        float z = 0.f;
+        for (int t = lane; t < T; t += 32) { const float e = expf(w[t] - mx); w[t] = e; z += e; }
+        z = warp_sum(z);
+        if (lane == 0) zs = z;
+    }
+    __syncthreads();
+    const float z = zs;
+    const int c = threadIdx.x * 4;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int t = 0; t < T; ++t) {
+        const float wt = w[t] / z;
+        const uint2 v = *reinterpret_cast<const uint2 *>(xp + (int64_t)t * D + c);
+        acc[0] += wt * bf16lo(v.x); acc[1] += wt * bf16hi(v.x); acc[2] += wt * bf16lo(v.y); acc[3] += wt * bf16hi(v.y);
+    }
+    *reinterpret_cast<uint2 *>(fo + c) = make_uint2(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]));
+}
+
+// ------------------------------------------------------------------ head
+// Warp per row of 2560: LN with affine, rounded to bf16, then ReLU on the bf16 value.
+__global__ void __launch_bounds__(256) k_ln_relu2560(bf16 *__restrict__ r, int64_t P, const float *__restrict__ g,
+                                                     const float *__restrict__ b) {
+    const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= P) return;
+    bf16 *xr = r + row * RED;
+    float v[80];
+#pragma unroll
+    for (int j = 0; j < 20; ++j) {
+        const uint2 q = *reinterpret_cast<const uint2 *>(xr + j * 128 + lane * 4);
+        v[4 * j] = bf16lo(q.x); v[4 * j + 1] = bf16hi(q.x); v[4 * j + 2] = bf16lo(q.y); v[4 * j + 3] = bf16hi(q.y);
+    }
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < 80; ++j) s += v[j];
+    const float mean = warp_sum(s) / (float)RED;
+    float q = 0.f;
+#pragma unroll
+    for (int j = 0; j < 80; ++j) { const float d = v[j] - mean; q += d * d; }
+    const float rstd = 1.f / sqrtf(warp_sum(q) / (float)RED + LN_EPS);
+#pragma unroll
+    for (int j = 0; j < 20; ++j) {
+        const int c = j * 128 + lane * 4;
+        uint32_t w2[2];
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const float o0 = (v[4 * j + 2 * k] - mean) * rstd * g[c + 2 * k] + b[c + 2 * k];
+            const float o1 = (v[4 * j + 2 * k + 1] - mean) * rstd * g[c + 2 * k + 1] + b[c + 2 * k + 1];
+            uint32_t u = pack_bf16x2(o0, o1);
+            if (u & 0x8000u) u &= 0xFFFF0000u;      // relu on the bf16 sign bit (tessera_cpu.cpp:570-571)
+            if (u & 0x80000000u) u &= 0x0000FFFFu;
+            w2[k] = u;
+        }
+        *reinterpret_cast<uint2 *>(xr + c) = make_uint2(w2[0], w2[1]);
+    }
+}
+
+// Warp per pixel: LN(128, no affine) -> bf16 -> f32 output or int8 quantisation.
+__global__ void __launch_bounds__(256) k_out128(const bf16 *__restrict__ r2, int64_t P, const uint8_t *__restrict__ empty,
+                                                float *__restrict__ out, int8_t *__restrict__ codes,
+                                                float *__restrict__ scales) {
+    const int64_t p = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (p >= P) return;
+    const uint2 q = *reinterpret_cast<const uint2 *>(r2 + p * OUT + lane * 4);
+    float v[4] = {bf16lo(q.x), bf16hi(q.x), bf16lo(q.y), bf16hi(q.y)};
+    const float mean = warp_sum(v[0] + v[1] + v[2] + v[3]) / (float)OUT;
+    float s = 0.f;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) { const float d = v[k] - mean; s += d * d; }
+    const float rstd = 1.f / sqrtf(warp_sum(s) / (float)OUT + LN_EPS);
+    const bool is_empty = empty && empty[p];
+    float e[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) e[k] = is_empty ? 0.f : bf16_round((v[k] - mean) * rstd);
+    if (out) {
+        *reinterpret_cast<float4 *>(out + p * OUT + lane * 4) = make_float4(e[0], e[1], e[2], e[3]);
+        return;
+    }
+    float am = fmaxf(fmaxf(fabsf(e[0]), fabsf(e[1])), fmaxf(fabsf(e[2]), fabsf(e[3])));
+    am = fmaxf(warp_max(am), 1e-12f);
+    const float sc = am / 127.0f;
+    uint32_t packed = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        float c = rintf(e[k] / sc);
+        c = fminf(127.f, fmaxf(-127.f, c));
+        packed |= (uint32_t)(uint8_t)(int8_t)(int)c << (8 * k);
+    }
+    *reinterpret_cast<uint32_t *>(codes + p * OUT + lane * 4) = packed;
+    if (lane == 0) scales[p] = sc;
+}
+
+// ------------------------------------------------------------------ launchers
+static unsigned blocks_for(int64_t n, int per_block) { return (unsigned)((n + per_block - 1) / per_block); }
+
+void launch_count(const TileDev &t, int64_t p0, int64_t np, int32_t *n2, int32_t *n1, cudaStream_t st) {
+    if (np <= 0) return;
+    k_count<<<blocks_for(np, 256), 256, 0, st>>>(t, p0, np, n2, n1);
+    check_launch("k_count");
+}
+
+void launch_gather(int modality, const TileDev &t, int64_t p0, int64_t np, const int32_t * /*nvalid*/,
+                   const int32_t *bins, Segs segs, float *rec, cudaStream_t st) {
+    if (np <= 0) return;
+    const int64_t steps = modality == 0 ? t.T2 : t.Ta + t.Td;
+    if (steps > MAX_STEPS) throw std::runtime_error("gather: series longer than " + std::to_string(MAX_STEPS));
+    if (modality == 0) k_gather<0><<<blocks_for(np, 4), 128, 0, st>>>(t, p0, np, bins, segs, rec);
+    else k_gather<1><<<blocks_for(np, 4), 128, 0, st>>>(t, p0, np, bins, segs, rec);
+    check_launch("k_gather");
+}
+
+void launch_emb1(int C, const float *rec, int64_t M, const float *w1t, const float *b1, bf16 *y, cudaStream_t st) {
+    if (M <= 0) return;
+    const unsigned grid = (unsigned)std::min<int64_t>(blocks_for(M, 8), 148 * 8);
+    if (C == 10) k_emb1<10><<<grid, 256, 0, st>>>(rec, M, w1t, b1, y);
+    else if (C == 2) k_emb1<2><<<grid, 256, 0, st>>>(rec, M, w1t, b1, y);
+    else throw std::runtime_error("emb1: unsupported band count");
+    check_launch("k_emb1");
+}
+
+void launch_attention(const bf16 *qkv, Segs segs, int64_t npix, int Tmax, bf16 *att, cudaStream_t st) {
+    if (npix <= 0 || Tmax <= 0) return;
+    if (Tmax > 256) throw std::runtime_error("attention: T > 256");
+    const int Tpad = (Tmax + 15) & ~15;
+    const size_t smem = (size_t)2 * Tpad * ATT_LD * sizeof(bf16);
+    static bool attr[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!attr[dev & 63]) {
+        cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, 2 * 256 * ATT_LD * 2);
+        attr[dev & 63] = true;
+    }
+    const int warps = std::min(8, Tpad / 16);
+    const dim3 grid((unsigned)npix, NH);
+    k_attention<<<grid, 32 * warps, smem, st>>>(qkv, segs, att, 1.f / std::sqrt((float)HD));
+    check_launch("k_attention");
+}
+
+void launch_layernorm640(const bf16 *x, int64_t M, const float *g, const float *b, bf16 *y, cudaStream_t st) {
+    if (M <= 0) return;
+    k_layernorm640<<<blocks_for(M, 8), 256, 0, st>>>(x, M, g, b, y);
+    check_launch("k_layernorm640");
+}
+
+void launch_pool(const bf16 *x, Segs segs, int64_t npix, const float *q, float qb, bf16 *fused, int col0,
+                 cudaStream_t st) {
+    if (npix <= 0) return;
+    k_pool<<<(unsigned)npix, 160, 0, st>>>(x, segs, q, qb, fused, col0);
+    check_launch("k_pool");
+}
+
+void launch_ln_relu2560(bf16 *r, int64_t P, const float *g, const float *b, cudaStream_t st) {
+    if (P <= 0) return;
+    k_ln_relu2560<<<blocks_for(P, 8), 256, 0, st>>>(r, P, g, b);
+    check_launch("k_ln_relu2560");
+}
+
+void launch_out128(const bf16 *r2, int64_t P, const uint8_t *empty, float *out, int8_t *codes, float *scales,
+                   cudaStream_t st) {
+    if (P <= 0) return;
+    k_out128<<<blocks_for(P, 8), 256, 0, st>>>(r2, P, empty, out, codes, scales);
+    check_launch("k_out128");
+}
+
+}  // namespace tcb

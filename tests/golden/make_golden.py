@@ -1,0 +1,162 @@
+"""Generate the golden fixtures of tests/golden/.
+
+  python tests/golden/make_golden.py padpattern
+      pad_pattern.npz: _pad_pattern(n, B) from numpy's own linspace /
+      array_split (the functions src/tessera_encode.cpp:157,169 mirror).
+  python tests/golden/make_golden.py driver
+      For each case tile: run the reference's unmodified driver
+      (oracle/_ref/tessera_encode_ref = src/tessera_encode.cpp + the CPU
+      back-end restatement) with TC_ORACLE_DUMP set. Stores <case>_batches.json
+      (per tc_encode call: G, T2, T1 and sha256 of the s2 / s1 records the
+      reference driver prepared) and <case>_oracle.npz (the codes and scales
+      it wrote).
+  python tests/golden/make_golden.py refcuda       (on a B200)
+      Runs the reference's unmodified driver + CUDA back end
+      (oracle/_ref/tessera_encode_cuda_ref, built by `make -C oracle cuda-ref`)
+      on the same case tiles: <case>_refcuda.npz. This is the reference's own
+      network arithmetic (cuBLASLt, bf16 biases) on the same inputs; it pins
+      the CPU restatement, which the test suite compares against it.
+
+Case tiles and weights are regenerated from seeds (tessera-inference_b200/synth.py).
+"""
+from __future__ import annotations
+
+import hashlib
+import json
+import os
+import struct
+import subprocess
+import sys
+import tempfile
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+REPO = HERE.parents[1]
+sys.path[:0] = [str(REPO / "tessera-inference_b200"), str(REPO / "oracle")]
+import synth  # noqa: E402
+
+# name -> (tile kwargs, weight perturbation)
+CASES = {
+    "cfg0": (dict(synth.CONFIGS[0]), 0.0),
+    "cloudy": (dict(H=32, W=32, T2=60, Ta=30, Td=30, p=0.15, seed=31, cloudy=True), 0.05),
+    "long": (dict(H=6, W=8, T2=300, Ta=150, Td=150, p=0.92, seed=32), 0.05),
+}
+
+
+def case_tile(name: str) -> dict:
+    return synth.make_tile(**CASES[name][0])
+
+
+def case_weights(name: str, wdir: Path) -> Path:
+    perturb = CASES[name][1]
+    return synth.make_weights(wdir / f"w_{perturb}.tcw", seed=0, perturb=perturb)
+
+
+def numpy_pad_pattern(n: int, B: int) -> np.ndarray:
+    if n == 0:
+        return np.zeros(B, np.int64)
+    if n >= B:
+        return np.linspace(0, n - 1, B, dtype=np.int64)
+    remain = B - n
+    if remain <= n:
+        extra = np.array([g[len(g) // 2] for g in np.array_split(np.arange(n), remain)], np.int64)
+    else:
+        extra = np.arange(remain) % n
+    return np.concatenate([np.arange(n), extra]).astype(np.int64)
+
+
+PAD_N = list(range(0, 41)) + [55, 63, 64, 65, 99, 100, 119, 120, 121, 127, 128, 129, 150, 199, 200, 201,
+                              255, 256, 257, 270, 300, 333, 1000]
+PAD_B = [1, 2, 3, 5, 8, 16, 24, 32, 40, 64, 72, 120, 128, 200, 248, 256]
+
+
+def padpattern():
+    keys, vals = [], []
+    for n in PAD_N:
+        for B in PAD_B:
+            keys.append((n, B))
+            vals.append(numpy_pad_pattern(n, B))
+    off = np.cumsum([0] + [len(v) for v in vals]).astype(np.int64)
+    np.savez_compressed(HERE / "pad_pattern.npz", nB=np.array(keys, np.int64), off=off,
+                        idx=np.concatenate(vals).astype(np.int16))
+    print("pad_pattern.npz:", len(keys), "cases")
+
+
+def read_dump(path: Path):
+    b = path.read_bytes()
+    G, T2, T1 = struct.unpack_from("<3q", b, 0)
+    o = 24
+    s2 = np.frombuffer(b, np.float32, G * T2 * 11, o); o += 4 * G * T2 * 11
+    s1 = np.frombuffer(b, np.float32, G * T1 * 3, o); o += 4 * G * T1 * 3
+    out = np.frombuffer(b, np.float32, G * 128, o)
+    return G, T2, T1, s2, s1, out
+
+
+def sha(a: np.ndarray) -> str:
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+
+def run_driver(binary: Path, name: str, work: Path, dump: bool):
+    tile = case_tile(name)
+    tdir = synth.write_tile_dir(tile, work / name / f"grid_{name}")
+    w = case_weights(name, work)
+    out = work / name / "out"
+    env = dict(os.environ)
+    dd = work / name / "dump"
+    if dump:
+        dd.mkdir(parents=True, exist_ok=True)
+        env["TC_ORACLE_DUMP"] = str(dd)
+    subprocess.run([str(binary), str(tdir), str(out), str(w)], check=True, env=env)
+    codes = np.load(out / f"grid_{name}.npy")
+    scales = np.load(out / f"grid_{name}_scales.npy")
+    batches, outs = [], []
+    if dump:
+        for f in sorted(dd.glob("batch_*.bin")):
+            G, T2, T1, s2, s1, o = read_dump(f)
+            batches.append({"G": G, "T2": T2, "T1": T1, "s2": sha(s2), "s1": sha(s1)})
+            outs.append(np.array(o).reshape(G, 128))
+    return codes, scales, batches, outs
+
+
+def driver():
+    binary = REPO / "oracle" / "_ref" / "tessera_encode_ref"
+    if not binary.exists():
+        sys.exit("build the reference driver first: make -C oracle")
+    with tempfile.TemporaryDirectory() as td:
+        for name in CASES:
+            codes, scales, batches, outs = run_driver(binary, name, Path(td), dump=True)
+            extra = {}
+            if name == "long":  # the f32 embeddings the driver quantised (pins the quantisation)
+                import oracle
+                emb = np.zeros((codes.shape[0] * codes.shape[1], 128), np.float32)
+                for (pix, _, _), o in zip(oracle.group_batches(case_tile(name)), outs):
+                    emb[pix] = o
+                extra["emb"] = emb
+            np.savez_compressed(HERE / f"{name}_oracle.npz", codes=codes, scales=scales, **extra)
+            (HERE / f"{name}_batches.json").write_text(json.dumps(batches, indent=0))
+            print(name, codes.shape, len(batches), "batches")
+
+
+def refcuda():
+    binary = REPO / "oracle" / "_ref" / "tessera_encode_cuda_ref"
+    if not binary.exists():
+        sys.exit("build the reference CUDA driver first: make -C oracle cuda-ref")
+    outdir = Path(os.environ.get("GOLDEN_OUT", HERE))
+    outdir.mkdir(parents=True, exist_ok=True)
+    with tempfile.TemporaryDirectory() as td:
+        for name in CASES:
+            codes, scales, _, _ = run_driver(binary, name, Path(td), dump=False)
+            np.savez_compressed(outdir / f"{name}_refcuda.npz", codes=codes, scales=scales)
+            print(name, codes.shape)
+
+
+if __name__ == "__main__":
+    cmd = sys.argv[1] if len(sys.argv) > 1 else "all"
+    if cmd in ("padpattern", "all"):
+        padpattern()
+    if cmd in ("driver", "all"):
+        driver()
+    if cmd == "refcuda":
+        refcuda()

@@ -1,0 +1,120 @@
+"""C-ABI checks that need no GPU: the library loads, exports every symbol the
+public headers declare, rejects bad weight files before touching CUDA, and
+plans FLOP-balanced row bands (the multi-GPU sharding) on the host."""
+import ctypes as C
+import re
+import struct
+
+import numpy as np
+import pytest
+
+import oracle
+import synth
+import tessera_b200 as tb
+from conftest import REPO
+
+
+def declared_functions():
+    names = set()
+    for h in (REPO / "include").glob("*.h"):
+        text = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
+        for m in re.finditer(r"^\s*[A-Za-z_][\w\s\*]*?\b(t[a-z]+_\w+)\s*\(", text, flags=re.M):
+            names.add(m.group(1))
+    return sorted(names)
+
+
+def test_headers_declare_reference_api():
+    names = declared_functions()
+    for n in ("tc_create", "tc_encode", "tc_profile_dump", "tc_destroy"):
+        assert n in names
+    assert len(names) >= 20
+
+
+def test_library_exports_every_declared_symbol():
+    lib = tb.load_library()
+    missing = [n for n in declared_functions() if not hasattr(lib, n)]
+    assert not missing, missing
+    assert set(declared_functions()) == set(tb.EXPORTED)
+
+
+def test_weights_rejected_before_cuda(tmp_path, capfd):
+    lib = tb.load_library()
+    bad = tmp_path / "bad.tcw"
+    bad.write_bytes(b"NOPE")
+    assert not lib.tc_create(str(bad).encode(), 4)
+    assert "tc_create: bad weights file" in capfd.readouterr().err
+    assert not lib.tc_create(str(tmp_path / "missing.tcw").encode(), 4)
+    assert "cannot open" in capfd.readouterr().err
+    # a well-formed file with a wrong shape names the tensor
+    w = synth.random_weights(0)
+    w["s2_backbone.embedding.2.weight"] = np.zeros((640, 639), np.float32)
+    p = tmp_path / "shape.tcw"
+    synth.write_tcw(p, w)
+    assert not lib.tc_create(str(p).encode(), 4)
+    assert "s2_backbone.embedding.2.weight" in capfd.readouterr().err
+    # truncated file
+    good = tmp_path / "good.tcw"
+    synth.write_tcw(good, synth.random_weights(0))
+    (tmp_path / "trunc.tcw").write_bytes(good.read_bytes()[:1000])
+    assert not lib.tc_create(str(tmp_path / "trunc.tcw").encode(), 4)
+    assert "truncated" in capfd.readouterr().err
+    w = synth.random_weights(0)
+    del w["dim_reducer.4.bias"]
+    synth.write_tcw(tmp_path / "miss.tcw", w)
+    assert not lib.tc_create(str(tmp_path / "miss.tcw").encode(), 4)
+    assert "missing tensor dim_reducer.4.bias" in capfd.readouterr().err
+
+
+def test_null_handle_errors(capfd):
+    lib = tb.load_library()
+    assert lib.tc_encode(None, None, 1, 8, None, 8, None) == -1
+    assert lib.tc_encode_tile(None, *([None] * 7), 1, 1, 1, 1, 1, None, None) == -1
+    lib.tc_destroy(None)
+    lib.tc_profile_dump(None)
+
+
+def test_tcw_roundtrip(tmp_path):
+    w = synth.random_weights(0, perturb=0.1)
+    p = tmp_path / "w.tcw"
+    synth.write_tcw(p, w)
+    r = synth.read_tcw(p)
+    assert list(r) == list(w)
+    for k in w:
+        np.testing.assert_array_equal(r[k], w[k])
+    b = p.read_bytes()
+    assert b[:4] == b"TCW1" and struct.unpack_from("<I", b, 4)[0] == 114
+
+
+def host_plan_reference(tile, nparts):
+    """Same rule as tc_plan_rows, in numpy: cut where the running FLOP sum
+    first reaches k/nparts of the total."""
+    T2, H, W = tile["masks"].shape
+    t2, t1 = oracle.tile_tokens(tile)
+    rows = oracle.pixel_flop(t2, t1).reshape(H, W).sum(1)
+    total, acc, k = rows.sum(), 0.0, 1
+    b = [0] + [H] * nparts
+    for r in range(H):
+        acc += rows[r]
+        while k < nparts and acc >= total * k / nparts:
+            b[k] = r + 1
+            k += 1
+    return b, rows
+
+
+@pytest.mark.parametrize("nparts", [1, 2, 3, 4, 8])
+def test_plan_rows_balanced(nparts):
+    tile = synth.make_tile(H=40, W=16, T2=30, Ta=12, Td=12, p=0.5, seed=41, cloudy=True)
+    b = tb.plan_rows(tile, nparts)
+    ref, rows = host_plan_reference(tile, nparts)
+    assert b == ref
+    assert b[0] == 0 and b[-1] == 40 and all(x <= y for x, y in zip(b, b[1:]))
+    share = [rows[b[i]:b[i + 1]].sum() for i in range(nparts)]
+    # each cut lands within one row of its target
+    assert max(share) - min(share) <= 2 * rows.max() + 1e-6 * rows.sum()
+
+
+def test_plan_rows_more_parts_than_rows():
+    tile = synth.make_tile(H=3, W=5, T2=8, Ta=4, Td=4, p=0.5, seed=42)
+    b = tb.plan_rows(tile, 8)
+    assert b[0] == 0 and b[-1] == 3 and len(b) == 9
+    assert all(x <= y for x, y in zip(b, b[1:]))
