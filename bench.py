@@ -1,0 +1,401 @@
+#!/usr/bin/env python3
+"""Benchmark of the B200 back end on the reference's headline workload.
+
+Metric: pixels/s (and tiles/hour) of the Tessera v2 Large
+pixel-student encoder. One step = one full encode of the workload tile: device
+binning, padding and standardisation, both backbones, the fusion head and the
+int8 quantisation, for every pixel.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference|refcuda]
+
+* N = 1: config 1, the Manchester-sized synthetic tile (1113 x 695 px,
+  T2 = 120 at 60% valid, Ta = Td = 60), seeded; Large weights random-init from
+  seed 0 (Xavier-uniform, zero biases).
+* N > 1 (under torchrun, one process per GPU): config 2, the same tile split by
+  pixel rows (FLOP-balanced) across the ranks; no inter-GPU traffic on the data
+  path (a barrier and a max-reduce of the timings only). Total work is fixed,
+  so scaling is "strong".
+* `value` is the whole-job throughput with the tile already resident in HBM;
+  `e2e` is the same through tc_encode_tile_rows with pinned host buffers
+  (host->device copy of the rank's rows and device->host copy of codes and
+  scales inside every timed step).
+* The tile (2.2 GB) is larger than the 126 MB L2, so no flush is needed
+  between steps.
+* --impl reference: the reference's own driver (src/tessera_encode.cpp,
+  unmodified) with the CPU back-end restatement (oracle/_ref/tessera_encode_ref)
+  on all host cores, on bounded pixel samples of the same tile; rank 0 only.
+* --impl refcuda: the reference's own driver + CUDA back end (cuBLASLt)
+  rebuilt for sm_100a (oracle/_ref/tessera_encode_cuda_ref) on one B200, on the
+  whole tile through its CLI (load from disk included, as the reference times it).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+REPO = Path(__file__).resolve().parent
+sys.path[:0] = [str(REPO / "tessera-inference_b200"), str(REPO / "oracle")]
+
+import synth  # noqa: E402
+
+METRIC = "pixels/sec (tiles/hour) per B200 and whole box at 1/2/4/8 GPUs vs ref CPU"
+UNIT = "px/s"
+WORKLOAD = "config 1: synthetic Manchester-sized tile 1113x695 (773,535 px), T2=120 (60% valid), Ta=Td=60"
+SMI_FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+REASONS = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+
+
+def measured_peaks() -> dict:
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16": d["bf16_tflops"], "bf16_sustained": d["bf16_tflops_sustained"],
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16": 1590.0, "bf16_sustained": 1400.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons of one GPU, sampled every 200 ms."""
+
+    def __init__(self, gpu_id: str):
+        self.gpu_id = gpu_id
+        self.proc = None
+        self.f = None
+
+    def __enter__(self):
+        self.f = tempfile.TemporaryFile(mode="w+")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={SMI_FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", self.gpu_id], stdout=self.f, stderr=subprocess.DEVNULL)
+        except FileNotFoundError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        if self.f is None:
+            return {}
+        self.f.seek(0)
+        sm, mx, reasons, n = [], 0.0, set(), 0
+        for line in self.f.read().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                s, m, pw = float(parts[1]), float(parts[2]), float(parts[3])
+            except ValueError:
+                continue
+            n += 1
+            mx = max(mx, m)
+            if pw > 200.0:  # under load
+                sm.append(s)
+            for name, v in zip(REASONS, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
+                "reasons": sorted(reasons), "samples": n, "samples_under_load": len(sm)}
+
+
+def weights_file(tmp: Path) -> Path:
+    return synth.make_weights(tmp / "student_large_seed0.tcw", seed=0)
+
+
+def band_arrays(tile: dict, r0: int, r1: int) -> dict:
+    """Rows [r0, r1) of every per-pixel array (all time steps), contiguous."""
+    out = dict(tile)
+    for k in ("bands", "masks", "asc", "desc"):
+        out[k] = np.ascontiguousarray(tile[k][:, r0:r1])
+    return out
+
+
+def tile_bytes(t: dict) -> int:
+    return sum(int(v.nbytes) for v in t.values())
+
+
+# ------------------------------------------------------------------ CPU reference arm
+def run_ref_driver(binary: Path, tile: dict, pixels: np.ndarray, weights: Path, work: Path, threads: int):
+    """Runs a reference driver binary on a 1 x K sub-tile; returns (wall s, ENCODE line)."""
+    sub = synth.subset_tile(tile, pixels)
+    tdir = synth.write_tile_dir(sub, work / "grid_sample")
+    env = dict(os.environ, OMP_NUM_THREADS=str(threads), OMP_PROC_BIND="close", OMP_WAIT_POLICY="ACTIVE",
+               TC_BLOCK="4", TC_BLOCK_S2="8", TC_BATCH="4096")
+    t0 = time.perf_counter()
+    r = subprocess.run([str(binary), str(tdir), str(work / "out"), str(weights)], env=env, capture_output=True,
+                       text=True, check=True)
+    wall = time.perf_counter() - t0
+    line = next((l for l in r.stdout.splitlines() if l.startswith("ENCODE")), "")
+    return wall, line
+
+
+def cpu_sample_px(binary, tile, weights, work, threads, target_s: float) -> tuple[int, float]:
+    """Calibrate a sample size (pixels) that takes about target_s on this host."""
+    N = tile["masks"].shape[1] * tile["masks"].shape[2]
+    wall, _ = run_ref_driver(binary, tile, np.arange(32), weights, work, threads)
+    rate = 32 / max(wall, 1e-3)
+    k = int(min(max(rate * target_s, 32), 20000, N))
+    return k, rate
+
+
+def cpu_reference_arm(args, tile, weights, work) -> dict:
+    binary = REPO / "oracle" / "_ref" / "tessera_encode_ref"
+    if not binary.exists():
+        return {"impl": "reference", "unavailable": f"{binary.relative_to(REPO)} not built (make -C oracle)"}
+    threads = os.cpu_count() or 1
+    k, _ = cpu_sample_px(binary, tile, weights, work, threads, target_s=args.cpu_step_s)
+    rng = np.random.default_rng(7)
+    N = tile["masks"].shape[1] * tile["masks"].shape[2]
+    samples = [np.sort(rng.choice(N, size=k, replace=False)) for _ in range(args.warmup + args.steps)]
+    for i in range(args.warmup):
+        run_ref_driver(binary, tile, samples[i], weights, work, threads)
+    walls = []
+    for i in range(args.steps):
+        w, line = run_ref_driver(binary, tile, samples[args.warmup + i], weights, work, threads)
+        walls.append(w)
+    pxs = k * args.steps / sum(walls)
+    sample = (f"{args.steps} steps of {k} random pixels of the config-1 tile each, run as 1x{k} tiles through the "
+              f"reference driver src/tessera_encode.cpp (unmodified; load, bin, prep, quant and write included) "
+              f"with the C++ restatement of the oneDNN CPU back end (oneDNN is not installed)")
+    cpu = {"value": pxs, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample,
+           "cpu_model": cpu_model()}
+    return {"metric": METRIC, "value": pxs, "unit": UNIT, "n_gpus": 0, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1000 * statistics.mean(walls), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "sample_px_per_step": k}, "impl": "reference",
+            "cpu_baseline": cpu, "tiles_per_hour": 3600 * pxs / 773535,
+            "e2e": {"value": pxs, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+# ------------------------------------------------------------------ reference CUDA arm
+def refcuda_arm(args, tile, weights, work) -> dict:
+    binary = REPO / "oracle" / "_ref" / "tessera_encode_cuda_ref"
+    if not binary.exists():
+        return {"impl": "refcuda", "unavailable": f"{binary.relative_to(REPO)} not built (make -C oracle cuda-ref)"}
+    tdir = synth.write_tile_dir(tile, work / "grid_cfg1")
+    best = None
+    for chunk in (64, 512, 1024):
+        env = dict(os.environ, TC_CHUNK=str(chunk), OMP_NUM_THREADS=str(os.cpu_count() or 1))
+        nets, totals = [], []
+        for i in range(args.warmup + args.steps):
+            r = subprocess.run([str(binary), str(tdir), str(work / "out"), str(weights)], env=env,
+                               capture_output=True, text=True, check=True)
+            line = next(l for l in r.stdout.splitlines() if l.startswith("ENCODE"))
+            if i >= args.warmup:
+                nets.append(float(re.search(r"net=([\d.]+)s", line).group(1)))
+                totals.append(float(re.search(r"total=([\d.]+)s", line).group(1)))
+        res = {"chunk": chunk, "net_s": statistics.median(nets), "total_s": statistics.median(totals)}
+        if best is None or res["total_s"] < best["total_s"]:
+            best = res
+    N = tile["masks"].shape[1] * tile["masks"].shape[2]
+    return {"metric": METRIC, "value": N / best["total_s"], "unit": UNIT, "n_gpus": 1, "impl": "refcuda",
+            "config": {"workload": WORKLOAD, "TC_CHUNK": best["chunk"]}, "net_px_s": N / best["net_s"],
+            "ms_per_step": 1000 * best["total_s"], "higher_is_better": True}
+
+
+# ------------------------------------------------------------------ B200 arm
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference", "refcuda"])
+    ap.add_argument("--config", type=int, default=1, choices=[0, 1, 3, 4])
+    ap.add_argument("--cpu-step-s", type=float, default=8.0, help="seconds per CPU reference sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile", action="store_true", help="print the per-category TCPROF table")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    work = Path(tempfile.mkdtemp(prefix="tcb_bench_"))
+    weights = weights_file(work)
+
+    if args.impl in ("reference", "refcuda"):
+        if rank != 0:
+            return
+        tile = synth.make_config_tile(args.config)
+        out = cpu_reference_arm(args, tile, weights, work) if args.impl == "reference" else refcuda_arm(
+            args, tile, weights, work)
+        print(json.dumps(out), flush=True)
+        return
+
+    import torch
+    import tessera_b200 as tb
+
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+
+    tile = synth.make_config_tile(args.config)
+    T2, H, W = tile["masks"].shape
+    Ta, Td = tile["asc"].shape[0], tile["desc"].shape[0]
+    bounds = tb.plan_rows(tile, world)
+    r0, r1 = bounds[rank], bounds[rank + 1]
+    band = band_arrays(tile, r0, r1)
+    R = r1 - r0
+    npx_band = R * W
+
+    enc = tb.Encoder(weights)
+    stream = torch.cuda.current_stream()
+    enc.set_stream(stream.cuda_stream)
+    dev = {k: torch.from_numpy(np.ascontiguousarray(v)).cuda() for k, v in band.items()}
+    codes_d = torch.empty((R, W, 128), dtype=torch.int8, device="cuda")
+    scales_d = torch.empty((R, W), dtype=torch.float32, device="cuda")
+
+    def step_device():
+        enc.encode_tile_device(dev, T2, Ta, Td, R, W, 0, R, codes_d, scales_d)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x: float) -> float:
+        if dist is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        step_device()
+    enc.reset_stats()
+    enc.set_profiling(True)
+    gpu_uuid = str(torch.cuda.get_device_properties(local).uuid)
+    gpu_id = gpu_uuid if gpu_uuid.startswith("GPU-") else f"GPU-{gpu_uuid}"
+    barrier()
+    with ClockSampler(gpu_id) as clocks:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            step_device()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        dev_ms = e0.elapsed_time(e1)
+    barrier()
+    st = enc.stats()
+    enc.set_profiling(False)
+    if args.profile:
+        enc.profile_dump()
+    dev_ms_max = max_over_ranks(dev_ms)
+
+    # end to end: host (pinned) -> device -> host, through tc_encode_tile_rows
+    pin = {k: torch.from_numpy(np.ascontiguousarray(v)).pin_memory() for k, v in band.items()}
+    pin_np = {k: v.numpy() for k, v in pin.items()}
+    codes_h = torch.empty((R, W, 128), dtype=torch.int8).pin_memory().numpy()
+    scales_h = torch.empty((R, W), dtype=torch.float32).pin_memory().numpy()
+    for _ in range(args.warmup):
+        enc.encode_tile(pin_np, 0, R, codes_h, scales_h)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        enc.encode_tile(pin_np, 0, R, codes_h, scales_h)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms_max = max_over_ranks(e0.elapsed_time(e1))
+    barrier()
+
+    # sanity: outputs of both paths agree and empty/valid pixels behave
+    ok = bool(np.array_equal(codes_d.cpu().numpy(), codes_h)) and bool(
+        np.array_equal(scales_d.cpu().numpy().view(np.uint32), scales_h.view(np.uint32)))
+
+    total_px = H * W
+    value = total_px * args.steps / (dev_ms_max / 1000.0)
+    e2e_value = total_px * args.steps / (e2e_ms_max / 1000.0)
+    h2d = tile_bytes(band)
+    d2h = npx_band * 128 + npx_band * 4
+
+    peaks = measured_peaks()
+    cat = st["ms_cat"]
+    gemm_ms = cat["gemm"]
+    gemm_tflops = st["gemm_flop"] / (gemm_ms * 1e-3) / 1e12 if gemm_ms > 0 else None
+    peak = peaks["bf16_sustained"]
+    alg_tflops = st["alg_flop"] / (dev_ms * 1e-3) / 1e12
+
+    if rank != 0:
+        if dist is not None:
+            dist.destroy_process_group()
+        return
+
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        binary = REPO / "oracle" / "_ref" / "tessera_encode_ref"
+        if binary.exists():
+            threads = os.cpu_count() or 1
+            k, _ = cpu_sample_px(binary, tile, weights, work, threads, target_s=15.0)
+            pix = np.sort(np.random.default_rng(8).choice(total_px, size=k, replace=False))
+            wall, _ = run_ref_driver(binary, tile, pix, weights, work, threads)
+            cpu = {"value": k / wall, "unit": UNIT, "cores": threads, "kind": "port",
+                   "sample": f"{k} random pixels of the config-1 tile as a 1x{k} tile through the reference driver "
+                             f"(unmodified) + C++ restatement of the oneDNN CPU back end, {wall:.1f} s",
+                   "cpu_model": cpu_model()}
+    out = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": dev_ms_max / args.steps, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": WORKLOAD if args.config == 1 else f"config {args.config}",
+                   "pixels": total_px, "split": f"rows FLOP-balanced over {world} GPU(s)",
+                   "weights": "Large, Xavier-uniform seed 0, zero biases",
+                   "l2": "inputs (2.2 GB tile) larger than L2; no flush"},
+        "tiles_per_hour": 3600.0 * value / total_px,
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world,
+                "tiles_per_hour": 3600.0 * e2e_value / total_px},
+        "gpu_launches": int(st["launches"]),
+        "roofline": {"bound": "tensor", "kernel": "k_gemm_bf16 (tcgen05)",
+                     "achieved": gemm_tflops, "peak": peak, "unit": "TFLOP/s",
+                     "frac": gemm_tflops / peak if gemm_tflops else None,
+                     "peak_source": f"{peaks['source']} bf16 sustained (kernel timed inside a long step)",
+                     "traffic": None,
+                     "end_to_end_tflops": alg_tflops, "end_to_end_frac": alg_tflops / peak},
+        "phase_ms_per_step": {k: v / args.steps for k, v in cat.items()},
+        "clocks": clocks.summary(),
+        "outputs_match_e2e": ok,
+    }
+    if cpu:
+        out["cpu_baseline"] = cpu
+    print(json.dumps(out), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
