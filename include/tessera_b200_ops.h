@@ -20,10 +20,11 @@ extern "C" {
  * src/tessera_cuda.cu:438-445 gemm). Residual: res (pitch ldr), or the DOY
  * sinusoid of pe_doy[row * pe_stride] looked up in pe_table (367 x 640 bf16,
  * src/tessera_cpu.cpp:503-509) with pe_div (320 f32) for non-table days.
- * bn = tile width (0 = automatic). */
+ * bn = tile width (0 = automatic); variant 0 = default kernel, 1 = single-CTA
+ * (M = 128 tiles), 2 = CTA pair (tcgen05 cta_group::2, M = 256 tiles). */
 int tcb_op_gemm(const void *A, int lda, const void *W, const float *bias, int relu, const void *res, int ldr,
                 const float *pe_doy, int pe_stride, const void *pe_table, const float *pe_div, void *out, int ldo,
-                int M, int N, int K, int bn, int *status, void *stream);
+                int M, int N, int K, int bn, int variant, int *status, void *stream);
 
 /* Valid-observation counts (src/tessera_encode.cpp:245-257) of pixels [p0, p0+np). */
 int tcb_op_count(const uint8_t *masks, const int16_t *asc, const int16_t *desc, int64_t T2, int64_t Ta, int64_t Td,

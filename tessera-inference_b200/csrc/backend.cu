@@ -865,7 +865,7 @@ void tc_destroy(void *handle) {
 
 int tcb_op_gemm(const void *A, int lda, const void *W, const float *bias, int relu, const void *res, int ldr,
                 const float *pe_doy, int pe_stride, const void *pe_table, const float *pe_div, void *out, int ldo, int M,
-                int N, int K, int bn, int *status, void *stream) {
+                int N, int K, int bn, int variant, int *status, void *stream) {
     OP_TRY("tcb_op_gemm", {
         GemmArgs p;
         p.M = M; p.N = N; p.K = K; p.bias = bias; p.relu = relu;
@@ -874,7 +874,7 @@ int tcb_op_gemm(const void *A, int lda, const void *W, const float *bias, int re
         p.pe_table = static_cast<const bf16 *>(pe_table); p.pe_div = pe_div;
         p.out = static_cast<bf16 *>(out); p.ldo = ldo; p.status = status;
         launch_gemm(p, static_cast<const bf16 *>(A), lda, static_cast<const bf16 *>(W),
-                    static_cast<cudaStream_t>(stream), bn);
+                    static_cast<cudaStream_t>(stream), bn, 0, variant);
     })
 }
 

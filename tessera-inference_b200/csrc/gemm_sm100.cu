@@ -20,6 +20,7 @@
 // The double-buffered accumulator lets the epilogue of tile i overlap the
 // main loop of tile i+1.
 #include <cstdio>
+#include <cstdlib>
 #include <mutex>
 #include <stdexcept>
 #include <string>
@@ -54,6 +55,88 @@ __device__ __forceinline__ float pe_value(float doy, int n, const bf16 *__restri
     if (tab) return __bfloat162float(table[di * D + n]);
     const float a = doy * div[n >> 1];
     return bf16_round((n & 1) ? cosf(a) : sinf(a));
+}
+
+// bias, [relu], residual or DOY sinusoid, bf16 rounding, 16-byte stores for
+// 16 accumulator columns of one output row.
+__device__ __forceinline__ void epilogue_cols16(const GemmArgs &p, const uint32_t (&r)[16], const uint4 (&res)[2],
+                                                bool has_res, float pe_doy, bool pe_tab, int pe_di, int n,
+                                                bf16 *out_row) {
+    float v[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
+    if (p.bias) {
+        const float4 *b4 = reinterpret_cast<const float4 *>(p.bias + n);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float4 b = __ldg(b4 + j);
+            v[4 * j] += b.x; v[4 * j + 1] += b.y; v[4 * j + 2] += b.z; v[4 * j + 3] += b.w;
+        }
+    }
+    if (p.relu) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[j] = fmaxf(v[j], 0.f);
+    }
+    if (has_res) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const uint32_t w[4] = {res[h].x, res[h].y, res[h].z, res[h].w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                v[8 * h + 2 * j] += bf16lo(w[j]);
+                v[8 * h + 2 * j + 1] += bf16hi(w[j]);
+            }
+        }
+    } else if (p.pe_doy) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[j] += pe_value(pe_doy, n + j, p.pe_table, p.pe_div, pe_tab, pe_di);
+    }
+    uint4 *dst = reinterpret_cast<uint4 *>(out_row + n);
+    dst[0] = make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]),
+                        pack_bf16x2(v[6], v[7]));
+    dst[1] = make_uint4(pack_bf16x2(v[8], v[9]), pack_bf16x2(v[10], v[11]), pack_bf16x2(v[12], v[13]),
+                        pack_bf16x2(v[14], v[15]));
+}
+
+// Epilogue of one BN-wide accumulator tile for the calling thread's output row
+// (TMEM lane). Every lane executes the TMEM loads; only rows < M touch memory.
+// Residual loads for a 32-column group are issued before its TMEM wait.
+template <int BN>
+__device__ __forceinline__ void epilogue_row(const GemmArgs &p, uint32_t tbase, int row, int n0) {
+    const bool live = row < p.M;
+    const bf16 *res_row = nullptr;
+    bool pe_tab = false;
+    int pe_di = 0;
+    float pe_doy = 0.f;
+    if (live) {
+        if (p.res) res_row = p.res + (size_t)row * p.ldr;
+        if (p.pe_doy) {
+            pe_doy = p.pe_doy[(size_t)row * p.pe_stride];
+            if (pe_doy >= 0.f && pe_doy <= 366.f && floorf(pe_doy) == pe_doy) {
+                pe_tab = true;
+                pe_di = (int)pe_doy;
+            }
+        }
+    }
+    bf16 *out_row = p.out + (size_t)row * p.ldo;
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 32) {
+        const bool two = c + 32 <= BN;
+        uint32_t r0[16], r1[16];
+        uint4 q0[2] = {}, q1[2] = {};
+        if (res_row) {
+            const uint4 *r4 = reinterpret_cast<const uint4 *>(res_row + n0 + c);
+            q0[0] = r4[0]; q0[1] = r4[1];
+            if (two) { q1[0] = r4[2]; q1[1] = r4[3]; }
+        }
+        tmem_ld16(tbase + (uint32_t)c, r0);
+        if (two) tmem_ld16(tbase + (uint32_t)(c + 16), r1);
+        tmem_ld_wait();
+        if (live) {
+            epilogue_cols16(p, r0, q0, res_row != nullptr, pe_doy, pe_tab, pe_di, n0 + c, out_row);
+            if (two) epilogue_cols16(p, r1, q1, res_row != nullptr, pe_doy, pe_tab, pe_di, n0 + c + 16, out_row);
+        }
+    }
 }
 
 template <int BN>
@@ -155,73 +238,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             const uint32_t use = (uint32_t)(tl >> 1);
             if (!mbar_wait(&tfull[buf], use & 1, abort_flag, p.status, ERR_WAIT_TMEM_FULL)) break;
             tc_fence_after();
-            const int row = m0 + row_in_tile;
-            const bool live = row < p.M;
-            // residual source for this row
-            const bf16 *res_row = nullptr;
-            bool pe_tab = false;
-            int pe_di = 0;
-            float pe_doy = 0.f;
-            if (live) {
-                if (p.res) res_row = p.res + (size_t)row * p.ldr;
-                if (p.pe_doy) {
-                    pe_doy = p.pe_doy[(size_t)row * p.pe_stride];
-                    if (pe_doy >= 0.f && pe_doy <= 366.f && floorf(pe_doy) == pe_doy) {
-                        pe_tab = true;
-                        pe_di = (int)pe_doy;
-                    }
-                }
-            }
-            bf16 *out_row = p.out + (size_t)row * p.ldo;
             const uint32_t tbase = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * BN);
-#pragma unroll 1
-            for (int c = 0; c < BN; c += 16) {
-                uint32_t r[16];
-                tmem_ld16(tbase + (uint32_t)c, r);
-                tmem_ld_wait();
-                if (live) {
-                    const int n = n0 + c;
-                    float v[16];
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
-                    if (p.bias) {
-                        const float4 *b4 = reinterpret_cast<const float4 *>(p.bias + n);
-#pragma unroll
-                        for (int j = 0; j < 4; ++j) {
-                            const float4 b = __ldg(b4 + j);
-                            v[4 * j] += b.x; v[4 * j + 1] += b.y; v[4 * j + 2] += b.z; v[4 * j + 3] += b.w;
-                        }
-                    }
-                    if (p.relu) {
-#pragma unroll
-                        for (int j = 0; j < 16; ++j) v[j] = fmaxf(v[j], 0.f);
-                    }
-                    if (res_row) {
-                        const uint4 *r4 = reinterpret_cast<const uint4 *>(res_row + n);
-#pragma unroll
-                        for (int h = 0; h < 2; ++h) {
-                            const uint4 q = r4[h];
-                            const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-                            for (int j = 0; j < 4; ++j) {
-                                v[8 * h + 2 * j] += bf16lo(w[j]);
-                                v[8 * h + 2 * j + 1] += bf16hi(w[j]);
-                            }
-                        }
-                    } else if (p.pe_doy) {
-#pragma unroll
-                        for (int j = 0; j < 16; ++j) v[j] += pe_value(pe_doy, n + j, p.pe_table, p.pe_div, pe_tab, pe_di);
-                    }
-                    uint4 o[2];
-                    o[0] = make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]),
-                                      pack_bf16x2(v[6], v[7]));
-                    o[1] = make_uint4(pack_bf16x2(v[8], v[9]), pack_bf16x2(v[10], v[11]), pack_bf16x2(v[12], v[13]),
-                                      pack_bf16x2(v[14], v[15]));
-                    uint4 *dst = reinterpret_cast<uint4 *>(out_row + n);
-                    dst[0] = o[0];
-                    dst[1] = o[1];
-                }
-            }
+            epilogue_row<BN>(p, tbase, m0 + row_in_tile, n0);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tempty[buf]);
@@ -232,6 +250,141 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     __syncthreads();
     tc_fence_after();
     if (warp == 1) tmem_dealloc(tmem_base, 512);
+}
+
+// ------------------------------------------------------------------ CTA-pair variant
+// tcgen05.mma.cta_group::2 with M = 256: a cluster of two CTAs computes a
+// 256 x BN tile. Each CTA loads its own 128 rows of A and half (BN/2 rows) of
+// W, so the W bytes a CTA moves per FLOP halve against the single-CTA kernel.
+// The leader (cluster rank 0) waits for both CTAs' bytes on its own "full"
+// barrier, issues the MMAs, and signals each CTA's "empty" and "tile full"
+// barriers with one commit per CTA. Each CTA's epilogue drains its own TMEM
+// (its 128 rows) and arrives on the leader's "tile empty" barrier.
+// No load uses cluster multicast.
+template <int BN> struct Gemm2Cfg {
+    static constexpr int BNH = BN / 2;
+    static constexpr int A_BYTES = BM * BK * 2;
+    static constexpr int B_BYTES = BNH * BK * 2;
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int STAGES_RAW = (SMEM_BUDGET - 2048) / STAGE_BYTES;
+    static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
+    static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256;
+    static_assert(BN % 16 == 0 && BN >= 32 && BN <= 256, "pair UMMA N must be a multiple of 16 in [32, 256]");
+    static_assert(B_BYTES % 1024 == 0, "B stage must keep 1024-byte alignment for the 128B swizzle");
+};
+
+template <int BN>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
+    k_gemm2_bf16(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs p) {
+    using Cfg = Gemm2Cfg<BN>;
+    constexpr int S = Cfg::STAGES;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *sA = smem;
+    uint8_t *sB = smem + S * Cfg::A_BYTES;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + S * Cfg::STAGE_BYTES);
+    uint64_t *full = bars, *empty = bars + S, *tfull = bars + 2 * S, *tempty = bars + 2 * S + 2;
+    uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 2 * S + 4);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+    const int num_n = p.N / BN;
+    const int num_m = (p.M + 2 * BM - 1) / (2 * BM);
+    const int ntiles = num_m * num_n;
+    const int nk = p.K / BK;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < S; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 1); }
+        for (int i = 0; i < 2; ++i) { mbar_init(&tfull[i], 1); mbar_init(&tempty[i], 8); }
+        *abort_flag = 0;
+        fence_mbar_init();
+        prefetch_tensormap(&tmA);
+        prefetch_tensormap(&tmB);
+    }
+    if (warp == 1) { tmem_alloc_pair(tmem_holder, 512); tmem_relinquish_pair(); }
+    tc_fence_before();
+    cluster_sync();  // both CTAs' barriers exist before any cross-CTA signal
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_holder;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int s = 0;
+            uint32_t ph = 0;
+            for (int t = pair; t < ntiles; t += npairs) {
+                const int m0 = (t / num_n) * (2 * BM) + (int)rank * BM;
+                const int n0 = (t % num_n) * BN + (int)rank * Cfg::BNH;
+                bool ok = true;
+                for (int kb = 0; kb < nk; ++kb) {
+                    if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, p.status, ERR_WAIT_SMEM_EMPTY)) { ok = false; break; }
+                    const uint32_t fbar = mapa_shared(smem_u32(&full[s]), 0);
+                    if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * Cfg::STAGE_BYTES);
+                    tma_load_2d_pair(sA + s * Cfg::A_BYTES, &tmA, kb * BK, m0, fbar);
+                    tma_load_2d_pair(sB + s * Cfg::B_BYTES, &tmB, kb * BK, n0, fbar);
+                    if (++s == S) { s = 0; ph ^= 1; }
+                }
+                if (!ok) break;
+            }
+            for (int i = 0; i < S; ++i) {  // tail: every stage released before exit
+                if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, p.status, ERR_WAIT_SMEM_EMPTY)) break;
+                if (++s == S) { s = 0; ph ^= 1; }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && rank == 0) {
+            constexpr uint32_t idesc = umma_idesc_bf16(2 * BM, BN);
+            int s = 0;
+            uint32_t ph = 0;
+            int tl = 0;
+            for (int t = pair; t < ntiles; t += npairs, ++tl) {
+                const int buf = tl & 1;
+                const uint32_t use = (uint32_t)(tl >> 1);
+                if (!mbar_wait(&tempty[buf], (use & 1) ^ 1, abort_flag, p.status, ERR_WAIT_TMEM_EMPTY)) break;
+                tc_fence_after();
+                const uint32_t d = tmem_base + (uint32_t)(buf * BN);
+                bool ok = true;
+                for (int kb = 0; kb < nk; ++kb) {
+                    if (!mbar_wait(&full[s], ph, abort_flag, p.status, ERR_WAIT_TMA_FULL)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint64_t adesc = umma_desc_sw128(smem_u32(sA + s * Cfg::A_BYTES));
+                    const uint64_t bdesc = umma_desc_sw128(smem_u32(sB + s * Cfg::B_BYTES));
+#pragma unroll
+                    for (int k = 0; k < BK / UMMA_K; ++k)
+                        umma_bf16_pair(d, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), idesc,
+                                       (kb | k) != 0 ? 1u : 0u);
+                    umma_commit_pair(mapa_shared(smem_u32(&empty[s]), 0));
+                    umma_commit_pair(mapa_shared(smem_u32(&empty[s]), 1));
+                    if (++s == S) { s = 0; ph ^= 1; }
+                }
+                if (!ok) break;
+                umma_commit_pair(mapa_shared(smem_u32(&tfull[buf]), 0));
+                umma_commit_pair(mapa_shared(smem_u32(&tfull[buf]), 1));
+            }
+        }
+    } else {
+        const int quad = warp & 3;
+        int tl = 0;
+        for (int t = pair; t < ntiles; t += npairs, ++tl) {
+            const int buf = tl & 1;
+            const uint32_t use = (uint32_t)(tl >> 1);
+            if (!mbar_wait(&tfull[buf], use & 1, abort_flag, p.status, ERR_WAIT_TMEM_FULL)) break;
+            tc_fence_after();
+            const int row = (t / num_n) * (2 * BM) + (int)rank * BM + quad * 32 + lane;
+            const uint32_t tbase = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * BN);
+            epilogue_row<BN>(p, tbase, row, (t % num_n) * BN);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[buf]), 0));
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();  // no CTA leaves while its peer may still signal its barriers or use its TMEM
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc_pair(tmem_base, 512);
 }
 
 // ------------------------------------------------------------------ host side
@@ -299,6 +452,37 @@ template <int BN> static void launch_bn(const GemmArgs &p, const bf16 *A, int ld
     k_gemm_bf16<BN><<<grid, GEMM_THREADS, Cfg::SMEM_BYTES, st>>>(ta, tb, p);
 }
 
+template <int BN> static void launch_pair(const GemmArgs &p, const bf16 *A, int lda, const bf16 *W, cudaStream_t st,
+                                          int max_ctas) {
+    using Cfg = Gemm2Cfg<BN>;
+    static bool attr_set[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!attr_set[dev & 63]) {
+        cudaError_t e =
+            cudaFuncSetAttribute(k_gemm2_bf16<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
+        if (e != cudaSuccess) throw std::runtime_error(std::string("gemm2 smem attribute: ") + cudaGetErrorString(e));
+        attr_set[dev & 63] = true;
+    }
+    CUtensorMap ta, tb;
+    make_tmap(&ta, A, (uint64_t)p.M, (uint64_t)p.K, (uint64_t)lda, BM);
+    make_tmap(&tb, W, (uint64_t)p.N, (uint64_t)p.K, (uint64_t)p.K, Cfg::BNH);
+    const int ntiles = ((p.M + 2 * BM - 1) / (2 * BM)) * (p.N / BN);
+    int pairs = std::min(ntiles, num_sms() / 2);
+    if (max_ctas > 0) pairs = std::min(pairs, std::max(1, max_ctas / 2));
+    if (pairs < 1) pairs = 1;
+    k_gemm2_bf16<BN><<<2 * pairs, GEMM_THREADS, Cfg::SMEM_BYTES, st>>>(ta, tb, p);
+}
+
+// TC_GEMM_VARIANT=1 forces the single-CTA kernel, 2 the CTA-pair kernel.
+int gemm_default_variant() {
+    static int v = [] {
+        const char *e = std::getenv("TC_GEMM_VARIANT");
+        return e && (*e == '1' || *e == '2') ? *e - '0' : 1;
+    }();
+    return v;
+}
+
 int gemm_pick_bn(int N) {
     if (N % 256 == 0) return 256;
     if (N % 240 == 0) return 240;
@@ -307,12 +491,23 @@ int gemm_pick_bn(int N) {
     return 0;
 }
 
-void launch_gemm(const GemmArgs &p, const bf16 *A, int lda, const bf16 *W, cudaStream_t st, int bn, int max_ctas) {
+void launch_gemm(const GemmArgs &p, const bf16 *A, int lda, const bf16 *W, cudaStream_t st, int bn, int max_ctas,
+                 int variant) {
     if (p.M <= 0) return;
     if (p.K % BK) throw std::runtime_error("gemm: K must be a multiple of 64");
     if (bn == 0) bn = gemm_pick_bn(p.N);
     if (bn == 0 || p.N % bn) throw std::runtime_error("gemm: unsupported N " + std::to_string(p.N));
     if (p.ldo % 8 || (p.res && p.ldr % 8)) throw std::runtime_error("gemm: output/residual pitch must be 16-byte aligned");
+    if (variant == 0) variant = gemm_default_variant();
+    if (variant == 2) {
+        switch (bn) {
+        case 256: launch_pair<256>(p, A, lda, W, st, max_ctas); return;
+        case 240: launch_pair<240>(p, A, lda, W, st, max_ctas); return;
+        case 160: launch_pair<160>(p, A, lda, W, st, max_ctas); return;
+        case 128: launch_pair<128>(p, A, lda, W, st, max_ctas); return;
+        default: throw std::runtime_error("gemm: unsupported pair tile width " + std::to_string(bn));
+        }
+    }
     switch (bn) {
     case 256: launch_bn<256>(p, A, lda, W, st, max_ctas); break;
     case 240: launch_bn<240>(p, A, lda, W, st, max_ctas); break;

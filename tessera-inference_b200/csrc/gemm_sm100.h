@@ -29,9 +29,14 @@ struct GemmArgs {
 // Tile width BN used for a given N (0 = unsupported).
 int gemm_pick_bn(int N);
 
+// Kernel used when launch_gemm is asked for variant 0: 1 = single CTA
+// (M = 128 tiles), 2 = CTA pair (cta_group::2, M = 256 tiles).
+int gemm_default_variant();
+
 // Enqueue one GEMM on `st`. bn = 0 picks the tile width; max_ctas > 0 caps the
-// persistent grid. Throws std::runtime_error on unsupported shapes.
+// persistent grid; variant 0 = default, 1 = single CTA, 2 = CTA pair.
+// Throws std::runtime_error on unsupported shapes.
 void launch_gemm(const GemmArgs &p, const __nv_bfloat16 *A, int lda, const __nv_bfloat16 *W, cudaStream_t st,
-                 int bn = 0, int max_ctas = 0);
+                 int bn = 0, int max_ctas = 0, int variant = 0);
 
 }  // namespace tcb

@@ -196,12 +196,23 @@ __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-// One CTA per (pixel, head). K and V of the head are staged in shared memory;
-// each warp owns 16 query rows: S = bf16(scale * Q K^T) over all keys, softmax
-// in f32 over the T valid keys, P rounded to bf16, O = bf16(P V)
+__device__ __forceinline__ void cp_async16(uint32_t smem_addr, const void *gptr) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr), "l"(gptr) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+    asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
+// One CTA per (pixel, head); NTMAX = key tiles of 8 the kernel is built for
+// (Tpad <= 8 * NTMAX). K and V of the head are staged in shared memory with
+// cp.async; each warp owns 16 query rows at a time:
+//   S = bf16(scale * Q K^T) over all keys, four independent key tiles in flight,
+//   softmax in f32 over the T valid keys (only tile padding is masked), P = bf16,
+//   O = bf16(P V) in two 80-column halves to bound register use
 // (tessera_cpu.cpp:333-343: matmul + linear post-op, softmax_accurate, matmul).
-__global__ void __launch_bounds__(256) k_attention(const bf16 *__restrict__ qkv, Segs segs, bf16 *__restrict__ att,
-                                                   float scale) {
+template <int NTMAX>
+__global__ void __launch_bounds__(256, NTMAX <= 16 ? 2 : 1)
+    k_attention(const bf16 *__restrict__ qkv, Segs segs, bf16 *__restrict__ att, float scale) {
     extern __shared__ __align__(16) uint8_t att_smem[];
     const int64_t i = blockIdx.x;
     const int h = blockIdx.y;
@@ -211,64 +222,82 @@ __global__ void __launch_bounds__(256) k_attention(const bf16 *__restrict__ qkv,
     const int Tpad = (T + 15) & ~15;
     bf16 *Ks = reinterpret_cast<bf16 *>(att_smem);
     bf16 *Vs = Ks + Tpad * ATT_LD;
-    const uint4 *qkv4 = reinterpret_cast<const uint4 *>(qkv);
+    const uint32_t ks_base = smem_u32(Ks), vs_base = smem_u32(Vs);
     for (int idx = threadIdx.x; idx < Tpad * (HD / 8); idx += blockDim.x) {
         const int r = idx / (HD / 8), c = idx % (HD / 8);
-        uint4 kk = make_uint4(0, 0, 0, 0), vv = kk;
+        const uint32_t off = (uint32_t)((r * ATT_LD + c * 8) * 2);
         if (r < T) {
-            const int64_t rb = (t0 + r) * (3 * D / 8);
-            kk = qkv4[rb + D / 8 + h * (HD / 8) + c];
-            vv = qkv4[rb + 2 * D / 8 + h * (HD / 8) + c];
+            const bf16 *row = qkv + (t0 + r) * (3 * D) + h * HD + c * 8;
+            cp_async16(ks_base + off, row + D);
+            cp_async16(vs_base + off, row + 2 * D);
+        } else {
+            *reinterpret_cast<uint4 *>(Ks + r * ATT_LD + c * 8) = make_uint4(0, 0, 0, 0);
+            *reinterpret_cast<uint4 *>(Vs + r * ATT_LD + c * 8) = make_uint4(0, 0, 0, 0);
         }
-        *reinterpret_cast<uint4 *>(Ks + r * ATT_LD + c * 8) = kk;
-        *reinterpret_cast<uint4 *>(Vs + r * ATT_LD + c * 8) = vv;
     }
-    __syncthreads();
-
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, tq = lane & 3;
     const int nwarps = blockDim.x >> 5;
     const int nrb = Tpad / 16, nnt = Tpad / 8;
-    const uint32_t ks_base = smem_u32(Ks), vs_base = smem_u32(Vs);
+    // Q fragments straight from global; the first row block's loads are in
+    // flight together with the K/V staging.
+    uint32_t qa[HD / 16][4];
+    auto load_q = [&](int rb) {
+        const int r0 = rb * 16 + g, r1 = r0 + 8;
+        const uint32_t *q0 = r0 < T ? reinterpret_cast<const uint32_t *>(qkv + (t0 + r0) * (3 * D) + h * HD) : nullptr;
+        const uint32_t *q1 = r1 < T ? reinterpret_cast<const uint32_t *>(qkv + (t0 + r1) * (3 * D) + h * HD) : nullptr;
+#pragma unroll
+        for (int ks = 0; ks < HD / 16; ++ks) {
+            qa[ks][0] = q0 ? __ldg(q0 + ks * 8 + tq) : 0u;
+            qa[ks][1] = q1 ? __ldg(q1 + ks * 8 + tq) : 0u;
+            qa[ks][2] = q0 ? __ldg(q0 + ks * 8 + 4 + tq) : 0u;
+            qa[ks][3] = q1 ? __ldg(q1 + ks * 8 + 4 + tq) : 0u;
+        }
+    };
+    if (warp < nrb) load_q(warp);
+    cp_async_wait_all();
+    __syncthreads();
     for (int rb = warp; rb < nrb; rb += nwarps) {
         const int r0 = rb * 16 + g, r1 = r0 + 8;
-        uint32_t qa[HD / 16][4];
-        {
-            const uint32_t *q0 = r0 < T ? reinterpret_cast<const uint32_t *>(qkv + (t0 + r0) * (3 * D) + h * HD) : nullptr;
-            const uint32_t *q1 = r1 < T ? reinterpret_cast<const uint32_t *>(qkv + (t0 + r1) * (3 * D) + h * HD) : nullptr;
-#pragma unroll
-            for (int ks = 0; ks < HD / 16; ++ks) {
-                qa[ks][0] = q0 ? __ldg(q0 + ks * 8 + tq) : 0u;
-                qa[ks][1] = q1 ? __ldg(q1 + ks * 8 + tq) : 0u;
-                qa[ks][2] = q0 ? __ldg(q0 + ks * 8 + 4 + tq) : 0u;
-                qa[ks][3] = q1 ? __ldg(q1 + ks * 8 + 4 + tq) : 0u;
-            }
-        }
+        if (rb != warp) load_q(rb);
         // S tiles, packed bf16: sp[nt][0] row r0 cols (nt*8 + 2tq, +1), sp[nt][1] row r1.
-        uint32_t sp[32][2];
+        uint32_t sp[NTMAX][2];
 #pragma unroll
-        for (int nt = 0; nt < 32; ++nt) {
-            if (nt < nnt) {
-                float c[4] = {0.f, 0.f, 0.f, 0.f};
-                const uint32_t addr = ks_base + (uint32_t)(((nt * 8 + (lane & 7)) * ATT_LD + (lane >> 3) * 8) * 2);
+        for (int nt0 = 0; nt0 < NTMAX; nt0 += 4) {
+            if (nt0 < nnt) {
+                float c[4][4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) c[j][0] = c[j][1] = c[j][2] = c[j][3] = 0.f;
 #pragma unroll
                 for (int ks = 0; ks < HD / 16; ks += 2) {
-                    uint32_t b0, b1, b2, b3;
-                    ldsm_x4(addr + ks * 32, b0, b1, b2, b3);
-                    mma_bf16_16816(c, qa[ks], b0, b1);
-                    mma_bf16_16816(c, qa[ks + 1], b2, b3);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        if (nt0 + j < nnt) {
+                            const uint32_t addr =
+                                ks_base + (uint32_t)((((nt0 + j) * 8 + (lane & 7)) * ATT_LD + (lane >> 3) * 8 + ks * 16) * 2);
+                            uint32_t b0, b1, b2, b3;
+                            ldsm_x4(addr, b0, b1, b2, b3);
+                            mma_bf16_16816(c[j], qa[ks], b0, b1);
+                            mma_bf16_16816(c[j], qa[ks + 1], b2, b3);
+                        }
+                    }
                 }
-                const int col = nt * 8 + 2 * tq;
-                const float ninf = -INFINITY;
-                const float s0 = col < T ? c[0] * scale : ninf, s1 = col + 1 < T ? c[1] * scale : ninf;
-                const float s2 = col < T ? c[2] * scale : ninf, s3 = col + 1 < T ? c[3] * scale : ninf;
-                sp[nt][0] = pack_bf16x2(s0, s1);
-                sp[nt][1] = pack_bf16x2(s2, s3);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    if (nt0 + j < NTMAX) {
+                        const int col = (nt0 + j) * 8 + 2 * tq;
+                        const float ninf = -INFINITY;
+                        const float s0 = col < T ? c[j][0] * scale : ninf, s1 = col + 1 < T ? c[j][1] * scale : ninf;
+                        const float s2 = col < T ? c[j][2] * scale : ninf, s3 = col + 1 < T ? c[j][3] * scale : ninf;
+                        sp[nt0 + j][0] = pack_bf16x2(s0, s1);
+                        sp[nt0 + j][1] = pack_bf16x2(s2, s3);
+                    }
+                }
             }
         }
         // softmax over keys: rows r0 (sp[.][0]) and r1 (sp[.][1]); a row lives in one lane quad
         float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
-        for (int nt = 0; nt < 32; ++nt)
+        for (int nt = 0; nt < NTMAX; ++nt)
             if (nt < nnt) {
                 mx0 = fmaxf(mx0, fmaxf(bf16lo(sp[nt][0]), bf16hi(sp[nt][0])));
                 mx1 = fmaxf(mx1, fmaxf(bf16lo(sp[nt][1]), bf16hi(sp[nt][1])));
@@ -280,7 +309,7 @@ __global__ void __launch_bounds__(256) k_attention(const bf16 *__restrict__ qkv,
         }
         float z0 = 0.f, z1 = 0.f;
 #pragma unroll
-        for (int nt = 0; nt < 32; ++nt)
+        for (int nt = 0; nt < NTMAX; ++nt)
             if (nt < nnt) {
                 z0 += expf(bf16lo(sp[nt][0]) - mx0) + expf(bf16hi(sp[nt][0]) - mx0);
                 z1 += expf(bf16lo(sp[nt][1]) - mx1) + expf(bf16hi(sp[nt][1]) - mx1);
@@ -292,76 +321,91 @@ __global__ void __launch_bounds__(256) k_attention(const bf16 *__restrict__ qkv,
         }
         const float inv0 = 1.f / z0, inv1 = 1.f / z1;
 #pragma unroll
-        for (int nt = 0; nt < 32; ++nt)
+        for (int nt = 0; nt < NTMAX; ++nt)
             if (nt < nnt) {
                 sp[nt][0] = pack_bf16x2(expf(bf16lo(sp[nt][0]) - mx0) * inv0, expf(bf16hi(sp[nt][0]) - mx0) * inv0);
                 sp[nt][1] = pack_bf16x2(expf(bf16lo(sp[nt][1]) - mx1) * inv1, expf(bf16hi(sp[nt][1]) - mx1) * inv1);
             }
-        // O = P V
-        float o[HD / 8][4];
+        // O = P V, in two halves of 80 columns
+        uint32_t *dst0 = r0 < T ? reinterpret_cast<uint32_t *>(att + (t0 + r0) * D + h * HD) : nullptr;
+        uint32_t *dst1 = r1 < T ? reinterpret_cast<uint32_t *>(att + (t0 + r1) * D + h * HD) : nullptr;
 #pragma unroll
-        for (int dn = 0; dn < HD / 8; ++dn) o[dn][0] = o[dn][1] = o[dn][2] = o[dn][3] = 0.f;
+        for (int half = 0; half < 2; ++half) {
+            float o[HD / 16][4];
 #pragma unroll
-        for (int kt = 0; kt < 16; ++kt) {
-            if (kt < nrb) {
-                const uint32_t a[4] = {sp[2 * kt][0], sp[2 * kt][1], sp[2 * kt + 1][0], sp[2 * kt + 1][1]};
-                const int vrow = kt * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
-                const uint32_t addr = vs_base + (uint32_t)((vrow * ATT_LD + (lane >> 4) * 8) * 2);
+            for (int dn = 0; dn < HD / 16; ++dn) o[dn][0] = o[dn][1] = o[dn][2] = o[dn][3] = 0.f;
 #pragma unroll
-                for (int dn2 = 0; dn2 < HD / 16; ++dn2) {
-                    uint32_t b0, b1, b2, b3;
-                    ldsm_x4_t(addr + dn2 * 32, b0, b1, b2, b3);
-                    mma_bf16_16816(o[2 * dn2], a, b0, b1);
-                    mma_bf16_16816(o[2 * dn2 + 1], a, b2, b3);
+            for (int kt = 0; kt < NTMAX / 2; ++kt) {
+                if (kt < nrb) {
+                    const uint32_t a[4] = {sp[2 * kt][0], sp[2 * kt][1], sp[2 * kt + 1][0], sp[2 * kt + 1][1]};
+                    const int vrow = kt * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+                    const uint32_t addr = vs_base + (uint32_t)((vrow * ATT_LD + half * (HD / 2) + (lane >> 4) * 8) * 2);
+#pragma unroll
+                    for (int dn2 = 0; dn2 < HD / 32; ++dn2) {
+                        uint32_t b0, b1, b2, b3;
+                        ldsm_x4_t(addr + dn2 * 32, b0, b1, b2, b3);
+                        mma_bf16_16816(o[2 * dn2], a, b0, b1);
+                        mma_bf16_16816(o[2 * dn2 + 1], a, b2, b3);
+                    }
                 }
             }
-        }
-        if (r0 < T) {
-            uint32_t *dst = reinterpret_cast<uint32_t *>(att + (t0 + r0) * D + h * HD);
+            if (dst0) {
 #pragma unroll
-            for (int dn = 0; dn < HD / 8; ++dn) dst[dn * 4 + tq] = pack_bf16x2(o[dn][0], o[dn][1]);
-        }
-        if (r1 < T) {
-            uint32_t *dst = reinterpret_cast<uint32_t *>(att + (t0 + r1) * D + h * HD);
+                for (int dn = 0; dn < HD / 16; ++dn) dst0[half * (HD / 4) + dn * 4 + tq] = pack_bf16x2(o[dn][0], o[dn][1]);
+            }
+            if (dst1) {
 #pragma unroll
-            for (int dn = 0; dn < HD / 8; ++dn) dst[dn * 4 + tq] = pack_bf16x2(o[dn][2], o[dn][3]);
+                for (int dn = 0; dn < HD / 16; ++dn) dst1[half * (HD / 4) + dn * 4 + tq] = pack_bf16x2(o[dn][2], o[dn][3]);
+            }
         }
     }
 }
 
 // ------------------------------------------------------------------ LayerNorm
-// Warp per row of 640: lane holds columns lane*4 + 128*j. Two-pass f32 stats.
+// Half-warp per row of 640: lane holds 8 columns at sub*8 + 128*j (16-byte
+// accesses). Two-pass f32 statistics.
+__device__ __forceinline__ float half_sum(float v) {
+#pragma unroll
+    for (int o = 8; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
 __global__ void __launch_bounds__(256) k_layernorm640(const bf16 *__restrict__ x, int64_t M, const float *__restrict__ g,
                                                       const float *__restrict__ b, bf16 *__restrict__ y) {
-    const int64_t r = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
-    const int lane = threadIdx.x & 31;
-    if (r >= M) return;
-    const bf16 *xr = x + r * D;
-    float v[20];
+    const int64_t r = (int64_t)blockIdx.x * 16 + (threadIdx.x >> 4);
+    const int sub = threadIdx.x & 15;
+    const bool live = r < M;
+    const bf16 *xr = x + (live ? r : 0) * D;
+    float v[40];
 #pragma unroll
     for (int j = 0; j < 5; ++j) {
-        const uint2 q = *reinterpret_cast<const uint2 *>(xr + j * 128 + lane * 4);
-        v[4 * j] = bf16lo(q.x); v[4 * j + 1] = bf16hi(q.x); v[4 * j + 2] = bf16lo(q.y); v[4 * j + 3] = bf16hi(q.y);
+        uint4 q = make_uint4(0, 0, 0, 0);
+        if (live) q = *reinterpret_cast<const uint4 *>(xr + j * 128 + sub * 8);
+        const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) { v[8 * j + 2 * k] = bf16lo(w[k]); v[8 * j + 2 * k + 1] = bf16hi(w[k]); }
     }
     float s = 0.f;
 #pragma unroll
-    for (int j = 0; j < 20; ++j) s += v[j];
-    const float mean = warp_sum(s) / (float)D;
+    for (int j = 0; j < 40; ++j) s += v[j];
+    const float mean = half_sum(s) / (float)D;
     float q = 0.f;
 #pragma unroll
-    for (int j = 0; j < 20; ++j) { const float d = v[j] - mean; q += d * d; }
-    const float rstd = 1.f / sqrtf(warp_sum(q) / (float)D + LN_EPS);
+    for (int j = 0; j < 40; ++j) { const float d = v[j] - mean; q += d * d; }
+    const float rstd = 1.f / sqrtf(half_sum(q) / (float)D + LN_EPS);
+    if (!live) return;
     bf16 *yr = y + r * D;
 #pragma unroll
     for (int j = 0; j < 5; ++j) {
-        const int c = j * 128 + lane * 4;
-        float o[4];
+        const int c = j * 128 + sub * 8;
+        float o[8];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            o[k] = (v[4 * j + k] - mean) * rstd;
-            if (g) o[k] = o[k] * g[c + k] + b[c + k];
+        for (int k = 0; k < 8; ++k) {
+            o[k] = (v[8 * j + k] - mean) * rstd;
+            if (g) o[k] = o[k] * __ldg(g + c + k) + __ldg(b + c + k);
         }
-        *reinterpret_cast<uint2 *>(yr + c) = make_uint2(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]));
+        *reinterpret_cast<uint4 *>(yr + c) = make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]),
+                                                        pack_bf16x2(o[4], o[5]), pack_bf16x2(o[6], o[7]));
     }
 }
 
@@ -518,27 +562,37 @@ void launch_emb1(int C, const float *rec, int64_t M, const float *w1t, const flo
     check_launch("k_emb1");
 }
 
-void launch_attention(const bf16 *qkv, Segs segs, int64_t npix, int Tmax, bf16 *att, cudaStream_t st) {
-    if (npix <= 0 || Tmax <= 0) return;
-    if (Tmax > 256) throw std::runtime_error("attention: T > 256");
-    const int Tpad = (Tmax + 15) & ~15;
-    const size_t smem = (size_t)2 * Tpad * ATT_LD * sizeof(bf16);
+template <int NT> static void attention_nt(const bf16 *qkv, Segs segs, int64_t npix, int Tpad, bf16 *att,
+                                          cudaStream_t st) {
     static bool attr[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (!attr[dev & 63]) {
-        cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, 2 * 256 * ATT_LD * 2);
+        cudaFuncSetAttribute(k_attention<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, 2 * 8 * NT * ATT_LD * 2);
         attr[dev & 63] = true;
     }
+    const size_t smem = (size_t)2 * Tpad * ATT_LD * sizeof(bf16);
     const int warps = std::min(8, Tpad / 16);
     const dim3 grid((unsigned)npix, NH);
-    k_attention<<<grid, 32 * warps, smem, st>>>(qkv, segs, att, 1.f / std::sqrt((float)HD));
+    k_attention<NT><<<grid, 32 * warps, smem, st>>>(qkv, segs, att, 1.f / std::sqrt((float)HD));
+}
+
+void launch_attention(const bf16 *qkv, Segs segs, int64_t npix, int Tmax, bf16 *att, cudaStream_t st) {
+    if (npix <= 0 || Tmax <= 0) return;
+    if (Tmax > 256) throw std::runtime_error("attention: T > 256");
+    const int Tpad = (Tmax + 15) & ~15;
+    if (Tpad <= 32) attention_nt<4>(qkv, segs, npix, Tpad, att, st);
+    else if (Tpad <= 64) attention_nt<8>(qkv, segs, npix, Tpad, att, st);
+    else if (Tpad <= 96) attention_nt<12>(qkv, segs, npix, Tpad, att, st);
+    else if (Tpad <= 128) attention_nt<16>(qkv, segs, npix, Tpad, att, st);
+    else if (Tpad <= 192) attention_nt<24>(qkv, segs, npix, Tpad, att, st);
+    else attention_nt<32>(qkv, segs, npix, Tpad, att, st);
     check_launch("k_attention");
 }
 
 void launch_layernorm640(const bf16 *x, int64_t M, const float *g, const float *b, bf16 *y, cudaStream_t st) {
     if (M <= 0) return;
-    k_layernorm640<<<blocks_for(M, 8), 256, 0, st>>>(x, M, g, b, y);
+    k_layernorm640<<<blocks_for(M, 16), 256, 0, st>>>(x, M, g, b, y);
     check_launch("k_layernorm640");
 }
 

@@ -83,7 +83,7 @@ def load_library(path: os.PathLike | None = None) -> C.CDLL:
     lib.tc_reset_stats.restype = None
     lib.tc_reset_stats.argtypes = [vp]
     lib.tcb_op_gemm.restype = i32
-    lib.tcb_op_gemm.argtypes = [vp, i32, vp, vp, i32, vp, i32, vp, i32, vp, vp, vp, i32, i32, i32, i32, i32, vp, vp]
+    lib.tcb_op_gemm.argtypes = [vp, i32, vp, vp, i32, vp, i32, vp, i32, vp, vp, vp, i32, i32, i32, i32, i32, i32, vp, vp]
     lib.tcb_op_count.restype = i32
     lib.tcb_op_count.argtypes = [vp, vp, vp, i64, i64, i64, i64, i64, i64, vp, vp, vp]
     lib.tcb_op_gather.restype = i32

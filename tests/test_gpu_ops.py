@@ -87,9 +87,10 @@ GEMM_SHAPES = [
 ]
 
 
+@pytest.mark.parametrize("variant", [1, 2])
 @pytest.mark.parametrize("M,N,K", GEMM_SHAPES)
 @pytest.mark.parametrize("mode", ["bias", "bias_relu", "bias_res"])
-def test_gemm(lib, M, N, K, mode):
+def test_gemm(lib, M, N, K, mode, variant):
     g = torch.Generator(device="cuda").manual_seed(M * 7 + N * 3 + K)
     A = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
     W = (torch.randn(N, K, device="cuda", generator=g) / K ** 0.5).to(torch.bfloat16)
@@ -99,7 +100,7 @@ def test_gemm(lib, M, N, K, mode):
     out = torch.full((M, N), float("nan"), device="cuda", dtype=torch.bfloat16)
     status = torch.zeros(1, dtype=torch.int32, device="cuda")
     rc = lib.tcb_op_gemm(_p(A), K, _p(W), _p(bias), int(relu), _p(res), N, None, 1, None, None, _p(out), N,
-                         M, N, K, 0, _p(status), _stream())
+                         M, N, K, 0, variant, _p(status), _stream())
     assert rc == 0
     torch.cuda.synchronize()
     assert status.item() == 0
@@ -107,15 +108,16 @@ def test_gemm(lib, M, N, K, mode):
     check_bf16(out, ref, mag)
 
 
+@pytest.mark.parametrize("variant", [1, 2])
 @pytest.mark.parametrize("bn", [128, 160, 256])
-def test_gemm_tile_widths(lib, bn):
+def test_gemm_tile_widths(lib, bn, variant):
     M, N, K = 1000, 1280, 640
     g = torch.Generator(device="cuda").manual_seed(bn)
     A = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
     W = (torch.randn(N, K, device="cuda", generator=g) / K ** 0.5).to(torch.bfloat16)
     out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
-    rc = lib.tcb_op_gemm(_p(A), K, _p(W), None, 0, None, 0, None, 1, None, None, _p(out), N, M, N, K, bn, None,
-                         _stream())
+    rc = lib.tcb_op_gemm(_p(A), K, _p(W), None, 0, None, 0, None, 1, None, None, _p(out), N, M, N, K, bn, variant,
+                         None, _stream())
     assert rc == 0
     torch.cuda.synchronize()
     ref, mag = gemm_ref(A, W, None, False, None)
@@ -140,7 +142,7 @@ def test_gemm_pe_residual(lib):
     rec[:, 2] = doy
     out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
     rc = lib.tcb_op_gemm(_p(A), K, _p(W), None, 0, None, 0, _p(rec[:, 2:]), 3, _p(table), _p(div), _p(out), N,
-                         M, N, K, 0, None, _stream())
+                         M, N, K, 0, 0, None, _stream())
     assert rc == 0
     torch.cuda.synchronize()
     angr = doy[:, None] * div[None, :]
