@@ -392,7 +392,7 @@ def main():
         "warmup": args.warmup, "ms_per_step": dev_ms_max / args.steps, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": WORKLOAD if args.config == 1 else f"config {args.config}",
-                   "chunk_tokens": int(os.environ.get("TC_CHUNK_TOKENS", "65536")),
+                   "chunk_tokens": int(os.environ.get("TC_CHUNK_TOKENS", "131072")),
                    "pixels": total_px, "split": f"rows FLOP-balanced over {world} GPU(s)",
                    "weights": "Large, Xavier-uniform seed 0, zero biases",
                    "l2": "inputs (2.2 GB tile) larger than L2; no flush"},
@@ -408,6 +408,8 @@ def main():
                      "traffic": None,
                      "end_to_end_tflops": alg_tflops, "end_to_end_frac": alg_tflops / peak},
         "phase_ms_per_step": cat, "profiled_step_ms": prof_ms,
+        "gemm_tflops_by_layer": {k: (v["flop"] / (v["ms"] * 1e-3) / 1e12 if v["ms"] > 0 else None)
+                                 for k, v in st["gemm_kind"].items()},
         "clocks": clocks.summary(),
         "outputs_match_e2e": ok,
     }

@@ -113,6 +113,9 @@ typedef struct {
     double gemm_launches;  /* number of GEMM launches */
     double launches;       /* number of kernel launches of this library */
     double ms_cat[TC_CAT_N]; /* per-category device time, only while profiling is on */
+    /* GEMM time and 2*M*N*K by layer (profiling on): emb2, QKV, out-proj, FFN1, FFN2, head */
+    double gemm_ms_kind[6];
+    double gemm_flop_kind[6];
 } tc_stats;
 
 /* Per-launch CUDA-event timing by category (adds one event per launch). */

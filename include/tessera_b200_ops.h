@@ -62,6 +62,12 @@ int tcb_op_ln_relu2560(void *r, int64_t P, const float *g, const float *b, void 
 int tcb_op_out128(const void *r2, int64_t P, const uint8_t *empty, float *out, int8_t *codes, float *scales,
                   void *stream);
 
+/* Failure-detection probe (no reference counterpart: the reference has no
+ * device-side waits). One kernel waits limit_us on an mbarrier that nothing
+ * signals, through the same bounded wait every pipeline kernel uses, then
+ * writes its error code (6) to *status and returns; the context stays usable. */
+int tcb_op_wait_probe(int64_t limit_us, int *status, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

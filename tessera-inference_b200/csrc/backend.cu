@@ -280,12 +280,19 @@ struct Dev {
         CK(cudaEventRecord(evpool[evn++], st));
     }
     // After a stream sync: attribute each gap between consecutive marks to the op that started it.
+    // GEMM marks carry 100 + layer kind.
     void harvest() {
         if (!prof || evn < 2) { evn = 0; return; }
         for (size_t i = 0; i + 1 < evn; ++i) {
             float ms = 0.f;
             CK(cudaEventElapsedTime(&ms, evpool[i], evpool[i + 1]));
-            stats.ms_cat[evcat[i]] += ms;
+            const int c = evcat[i];
+            if (c >= 100) {
+                stats.ms_cat[TC_CAT_GEMM] += ms;
+                stats.gemm_ms_kind[c - 100] += ms;
+            } else {
+                stats.ms_cat[c] += ms;
+            }
         }
         evn = 0;
     }
@@ -309,7 +316,7 @@ static void dev_init(Dev &d, int device, const Blob &blob, const ModelOff &off) 
     CK(cudaMalloc(&d.wdev, blob.bytes.size()));
     CK(cudaMemcpy(d.wdev, blob.bytes.data(), blob.bytes.size(), cudaMemcpyHostToDevice));
     d.m = model_at(d.wdev, off);
-    d.tok_cap = env_int("TC_CHUNK_TOKENS", 65536);
+    d.tok_cap = env_int("TC_CHUNK_TOKENS", 131072);
     d.px_cap = env_int("TC_CHUNK_PIXELS", 8192);
     d.status.ensure(1);
     CK(cudaMemset(d.status.p, 0, sizeof(int)));
@@ -321,10 +328,12 @@ static void dev_init(Dev &d, int device, const Blob &blob, const ModelOff &off) 
 }
 
 // ------------------------------------------------------------------ forward pass
-static void gemm(Dev &d, const Lin &L, const bf16 *A, int64_t M, bf16 *out, bool relu, const bf16 *res = nullptr,
-                 const float *pe_doy = nullptr, int pe_stride = 1) {
+enum GemmKind { GK_EMB2 = 0, GK_QKV, GK_OUT, GK_FFN1, GK_FFN2, GK_HEAD };
+
+static void gemm(Dev &d, int kind, const Lin &L, const bf16 *A, int64_t M, bf16 *out, bool relu,
+                 const bf16 *res = nullptr, const float *pe_doy = nullptr, int pe_stride = 1) {
     if (M <= 0) return;
-    d.mark(TC_CAT_GEMM);
+    d.mark(100 + kind);
     GemmArgs p;
     p.M = (int)M;
     p.N = L.N;
@@ -342,6 +351,7 @@ static void gemm(Dev &d, const Lin &L, const bf16 *A, int64_t M, bf16 *out, bool
     p.status = d.status.p;
     launch_gemm(p, A, L.K, L.w, d.st);
     d.stats.gemm_flop += 2.0 * double(M) * L.N * L.K;
+    d.stats.gemm_flop_kind[kind] += 2.0 * double(M) * L.N * L.K;
     d.stats.gemm_launches += 1;
     d.stats.launches += 1;
 }
@@ -354,16 +364,16 @@ static void backbone(Dev &d, int b, const float *rec, Segs segs, int64_t M, int 
         d.mark(TC_CAT_EMB1);
         launch_emb1(B.C, rec, M, B.w1t, B.b1, d.y.p, d.st);
         d.stats.launches += 1;
-        gemm(d, B.emb2, d.y.p, M, d.x.p, false, nullptr, rec + B.C, B.C + 1);  // + DOY sinusoid
+        gemm(d, GK_EMB2, B.emb2, d.y.p, M, d.x.p, false, nullptr, rec + B.C, B.C + 1);  // + DOY sinusoid
         for (int l = 0; l < NL; ++l) {
-            gemm(d, B.qkv[l], d.x.p, M, d.qkv.p, false);
+            gemm(d, GK_QKV, B.qkv[l], d.x.p, M, d.qkv.p, false);
             d.mark(TC_CAT_ATTN);
             launch_attention(d.qkv.p, segs, npix, Tmax, d.att.p, d.st);
-            gemm(d, B.out[l], d.att.p, M, d.y.p, false, d.x.p);
+            gemm(d, GK_OUT, B.out[l], d.att.p, M, d.y.p, false, d.x.p);
             d.mark(TC_CAT_LN);
             launch_layernorm640(d.y.p, M, B.ln1g[l], B.ln1b[l], d.x1.p, d.st);
-            gemm(d, B.ffn1[l], d.x1.p, M, d.hbuf.p, true);
-            gemm(d, B.ffn2[l], d.hbuf.p, M, d.y.p, false, d.x1.p);
+            gemm(d, GK_FFN1, B.ffn1[l], d.x1.p, M, d.hbuf.p, true);
+            gemm(d, GK_FFN2, B.ffn2[l], d.hbuf.p, M, d.y.p, false, d.x1.p);
             d.mark(TC_CAT_LN);
             launch_layernorm640(d.y.p, M, B.ln2g[l], B.ln2b[l], d.x.p, d.st);
             d.stats.launches += 3;
@@ -376,10 +386,10 @@ static void backbone(Dev &d, int b, const float *rec, Segs segs, int64_t M, int 
 }
 
 static void head(Dev &d, int64_t npix, const uint8_t *empty, float *outf, int8_t *codes, float *scales) {
-    gemm(d, d.m.red1, d.fused.p, npix, d.r1.p, false);
+    gemm(d, GK_HEAD, d.m.red1, d.fused.p, npix, d.r1.p, false);
     d.mark(TC_CAT_HEAD);
     launch_ln_relu2560(d.r1.p, npix, d.m.rlng, d.m.rlnb, d.st);
-    gemm(d, d.m.red2, d.r1.p, npix, d.r2.p, false);
+    gemm(d, GK_HEAD, d.m.red2, d.r1.p, npix, d.r2.p, false);
     d.mark(TC_CAT_HEAD);
     launch_out128(d.r2.p, npix, empty, outf, codes, scales, d.st);
     d.stats.launches += 2;
@@ -812,6 +822,10 @@ int tc_get_stats(void *handle, tc_stats *out) {
         out->gemm_launches += s.gemm_launches;
         out->launches += s.launches;
         for (int k = 0; k < TC_CAT_N; ++k) out->ms_cat[k] += s.ms_cat[k];
+        for (int k = 0; k < 6; ++k) {
+            out->gemm_ms_kind[k] += s.gemm_ms_kind[k];
+            out->gemm_flop_kind[k] += s.gemm_flop_kind[k];
+        }
     }
     return 0;
 }
@@ -841,6 +855,11 @@ void tc_profile_dump(void *handle) {
         if (s.ms_cat[TC_CAT_GEMM] > 0)
             std::printf("TCPROF GEMM throughput %.1f TFLOP/s over %.3g FLOP\n",
                         s.gemm_flop / (s.ms_cat[TC_CAT_GEMM] * 1e-3) / 1e12, s.gemm_flop);
+        static const char *kinds[6] = {"emb2+DOY", "QKV", "out-proj+res", "FFN1+ReLU", "FFN2+res", "head"};
+        for (int k = 0; k < 6; ++k)
+            if (s.gemm_ms_kind[k] > 0)
+                std::printf("TCPROF   GEMM %-13s %9.2f ms %7.1f TFLOP/s\n", kinds[k], s.gemm_ms_kind[k],
+                            s.gemm_flop_kind[k] / (s.gemm_ms_kind[k] * 1e-3) / 1e12);
     } else {
         std::printf("TCPROF per-category timing disabled (tc_set_profiling)\n");
     }
@@ -928,6 +947,11 @@ int tcb_op_out128(const void *r2, int64_t P, const uint8_t *empty, float *out, i
                   void *stream) {
     OP_TRY("tcb_op_out128", launch_out128(static_cast<const bf16 *>(r2), P, empty, out, codes, scales,
                                           static_cast<cudaStream_t>(stream)))
+}
+
+int tcb_op_wait_probe(int64_t limit_us, int *status, void *stream) {
+    OP_TRY("tcb_op_wait_probe", launch_wait_probe((uint64_t)std::max<int64_t>(limit_us, 0) * 1000, status,
+                                                  static_cast<cudaStream_t>(stream)))
 }
 
 }  // extern "C"

@@ -28,6 +28,7 @@ enum : int {
     ERR_WAIT_TMEM_FULL = 3,
     ERR_WAIT_TMEM_EMPTY = 4,
     ERR_BAD_SEGMENT = 5,
+    ERR_WAIT_PROBE = 6,
 };
 
 // Wall-clock limit of one mbarrier wait (ns). Far above any legitimate wait.
@@ -77,13 +78,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
 // (and leaves the CTA abort flag raised) if it gave up, either because this
 // wait ran out of time or because another role of the CTA already aborted.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag, int *status,
-                                          int code) {
+                                          int code, uint64_t limit_ns = WAIT_LIMIT_NS) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
     while (true) {
         if (mbar_try_wait(bar, parity)) return true;
         if (*abort_flag) return false;
-        if (globaltimer_ns() - t0 > WAIT_LIMIT_NS) {
+        if (globaltimer_ns() - t0 > limit_ns) {
             *abort_flag = 1;
             if (status) atomicCAS(status, 0, code);
             return false;

@@ -14,9 +14,10 @@
 //   warp 1      TMEM allocator and MMA issuer: one elected thread issues
 //               tcgen05.mma (M=128, N=BN, K=16) into a double-buffered f32
 //               accumulator in tensor memory and commits stage/tile barriers.
-//   warps 2-5   epilogue: tcgen05.ld of the accumulator (one TMEM lane
-//               quadrant per warp, one output row per thread), bias, ReLU,
-//               residual, bf16 rounding, 16-byte stores.
+//   warps 2-9   epilogue: tcgen05.ld of the accumulator (two warps per TMEM
+//               lane quadrant, splitting the columns; one output row per
+//               lane), bias, ReLU, residual, bf16 rounding, then a swizzled
+//               shared-memory staging buffer and row-contiguous global stores.
 // The double-buffered accumulator lets the epilogue of tile i overlap the
 // main loop of tile i+1.
 #include <cstdio>
@@ -35,16 +36,18 @@ namespace tcb {
 constexpr int BM = 128;           // UMMA M (cta_group::1)
 constexpr int BK = 64;            // one 128-byte swizzle atom of bf16 along K
 constexpr int UMMA_K = 16;        // K per tcgen05.mma for 16-bit inputs
-constexpr int GEMM_THREADS = 192; // 6 warps
+constexpr int GEMM_THREADS = 320; // 10 warps: producer, MMA, 8 epilogue
+constexpr int EPI_WARPS = 8;      // two per TMEM lane quadrant, splitting the tile's columns
+constexpr int STAGING_BYTES = EPI_WARPS * 32 * 64;  // per epilogue warp: 32 rows x 32 bf16
 constexpr int SMEM_BUDGET = 225 * 1024;
 
 template <int BN> struct GemmCfg {
     static constexpr int A_BYTES = BM * BK * 2;
     static constexpr int B_BYTES = BN * BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int STAGES_RAW = (SMEM_BUDGET - 2048) / STAGE_BYTES;
+    static constexpr int STAGES_RAW = (SMEM_BUDGET - 2048 - STAGING_BYTES) / STAGE_BYTES;
     static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
-    static constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * STAGE_BYTES + 256 /*barriers*/;
+    static constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * STAGE_BYTES + STAGING_BYTES + 256 /*barriers*/;
     static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N for M=128 must be a multiple of 16 in [16,256]");
     static_assert(B_BYTES % 1024 == 0, "B stage must keep 1024-byte alignment for the 128B swizzle");
     static_assert(STAGES >= 2, "need at least two pipeline stages");
@@ -57,11 +60,11 @@ __device__ __forceinline__ float pe_value(float doy, int n, const bf16 *__restri
     return bf16_round((n & 1) ? cosf(a) : sinf(a));
 }
 
-// bias, [relu], residual or DOY sinusoid, bf16 rounding, 16-byte stores for
-// 16 accumulator columns of one output row.
+// bias, [relu], residual or DOY sinusoid and bf16 rounding of 16 accumulator
+// columns of one output row, packed into two 16-byte words.
 __device__ __forceinline__ void epilogue_cols16(const GemmArgs &p, const uint32_t (&r)[16], const uint4 (&res)[2],
                                                 bool has_res, float pe_doy, bool pe_tab, int pe_di, int n,
-                                                bf16 *out_row) {
+                                                uint4 (&o)[2]) {
     float v[16];
 #pragma unroll
     for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
@@ -91,18 +94,22 @@ __device__ __forceinline__ void epilogue_cols16(const GemmArgs &p, const uint32_
 #pragma unroll
         for (int j = 0; j < 16; ++j) v[j] += pe_value(pe_doy, n + j, p.pe_table, p.pe_div, pe_tab, pe_di);
     }
-    uint4 *dst = reinterpret_cast<uint4 *>(out_row + n);
-    dst[0] = make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]),
-                        pack_bf16x2(v[6], v[7]));
-    dst[1] = make_uint4(pack_bf16x2(v[8], v[9]), pack_bf16x2(v[10], v[11]), pack_bf16x2(v[12], v[13]),
-                        pack_bf16x2(v[14], v[15]));
+    o[0] = make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]),
+                      pack_bf16x2(v[6], v[7]));
+    o[1] = make_uint4(pack_bf16x2(v[8], v[9]), pack_bf16x2(v[10], v[11]), pack_bf16x2(v[12], v[13]),
+                      pack_bf16x2(v[14], v[15]));
 }
 
-// Epilogue of one BN-wide accumulator tile for the calling thread's output row
-// (TMEM lane). Every lane executes the TMEM loads; only rows < M touch memory.
-// Residual loads for a 32-column group are issued before its TMEM wait.
-template <int BN>
-__device__ __forceinline__ void epilogue_row(const GemmArgs &p, uint32_t tbase, int row, int n0) {
+// One epilogue warp: output rows row_base .. row_base + 31 (its TMEM lane
+// quadrant, one row per lane) and accumulator columns [c0, c1) of a tile whose
+// first output column is n0. Per group of 32 columns: TMEM -> registers ->
+// epilogue math -> a 2 KB staging buffer (32 rows x 64 B, 16-byte chunks XOR-
+// swizzled so both the row-wise writes and the read-back are conflict-free) ->
+// row-contiguous 64-byte global stores, 8 rows per instruction. Residual loads
+// for a group are issued before its TMEM wait.
+__device__ __forceinline__ void epilogue_span(const GemmArgs &p, uint32_t tbase, int row_base, int n0, int c0, int c1,
+                                              uint8_t *stage, int lane) {
+    const int row = row_base + lane;
     const bool live = row < p.M;
     const bf16 *res_row = nullptr;
     bool pe_tab = false;
@@ -118,10 +125,11 @@ __device__ __forceinline__ void epilogue_row(const GemmArgs &p, uint32_t tbase, 
             }
         }
     }
-    bf16 *out_row = p.out + (size_t)row * p.ldo;
+    uint4 *my_row = reinterpret_cast<uint4 *>(stage + lane * 64);
+    const int sw = (lane >> 1) & 3;
 #pragma unroll 1
-    for (int c = 0; c < BN; c += 32) {
-        const bool two = c + 32 <= BN;
+    for (int c = c0; c < c1; c += 32) {
+        const bool two = c + 32 <= c1;
         uint32_t r0[16], r1[16];
         uint4 q0[2] = {}, q1[2] = {};
         if (res_row) {
@@ -132,12 +140,40 @@ __device__ __forceinline__ void epilogue_row(const GemmArgs &p, uint32_t tbase, 
         tmem_ld16(tbase + (uint32_t)c, r0);
         if (two) tmem_ld16(tbase + (uint32_t)(c + 16), r1);
         tmem_ld_wait();
-        if (live) {
-            epilogue_cols16(p, r0, q0, res_row != nullptr, pe_doy, pe_tab, pe_di, n0 + c, out_row);
-            if (two) epilogue_cols16(p, r1, q1, res_row != nullptr, pe_doy, pe_tab, pe_di, n0 + c + 16, out_row);
+        uint4 o[2];
+        epilogue_cols16(p, r0, q0, res_row != nullptr, pe_doy, pe_tab, pe_di, n0 + c, o);
+        my_row[0 ^ sw] = o[0];
+        my_row[1 ^ sw] = o[1];
+        if (two) {
+            epilogue_cols16(p, r1, q1, res_row != nullptr, pe_doy, pe_tab, pe_di, n0 + c + 16, o);
+            my_row[2 ^ sw] = o[0];
+            my_row[3 ^ sw] = o[1];
         }
+        __syncwarp();
+        if (two) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int rr = i * 8 + (lane >> 2), k = lane & 3;
+                const uint4 v = reinterpret_cast<const uint4 *>(stage + rr * 64)[k ^ ((rr >> 1) & 3)];
+                if (row_base + rr < p.M)
+                    *reinterpret_cast<uint4 *>(p.out + (size_t)(row_base + rr) * p.ldo + n0 + c + k * 8) = v;
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+                const int rr = i * 16 + (lane >> 1), k = lane & 1;
+                const uint4 v = reinterpret_cast<const uint4 *>(stage + rr * 64)[k ^ ((rr >> 1) & 3)];
+                if (row_base + rr < p.M)
+                    *reinterpret_cast<uint4 *>(p.out + (size_t)(row_base + rr) * p.ldo + n0 + c + k * 8) = v;
+            }
+        }
+        __syncwarp();
     }
 }
+
+// Column split of a BN-wide tile between the two epilogue warps of a quadrant
+// (at a multiple of 32 near the middle).
+template <int BN> __host__ __device__ constexpr int epi_split() { return ((BN / 2 + 16) / 32) * 32; }
 
 template <int BN>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
@@ -148,7 +184,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *sA = smem;
     uint8_t *sB = smem + S * Cfg::A_BYTES;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + S * Cfg::STAGE_BYTES);
+    uint8_t *staging = smem + S * Cfg::STAGE_BYTES;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(staging + STAGING_BYTES);
     uint64_t *full = bars, *empty = bars + S, *tfull = bars + 2 * S, *tempty = bars + 2 * S + 2;
     uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 2 * S + 4);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
@@ -161,7 +198,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < S; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 1); }
-        for (int i = 0; i < 2; ++i) { mbar_init(&tfull[i], 1); mbar_init(&tempty[i], 4); }
+        for (int i = 0; i < 2; ++i) { mbar_init(&tfull[i], 1); mbar_init(&tempty[i], EPI_WARPS); }
         *abort_flag = 0;
         fence_mbar_init();
         prefetch_tensormap(&tmA);
@@ -228,9 +265,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             }
         }
     } else {
-        // epilogue warps 2..5: TMEM lane quadrant = warp % 4
-        const int quad = warp & 3;
-        const int row_in_tile = quad * 32 + lane;
+        // epilogue warps 2..9: TMEM lane quadrant = warp % 4, column half = (warp - 2) / 4
+        const int quad = warp & 3, e = warp - 2, half = e >> 2;
+        const int c0 = half ? epi_split<BN>() : 0, c1 = half ? BN : epi_split<BN>();
+        uint8_t *stage = staging + e * (32 * 64);
         int tl = 0;
         for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++tl) {
             const int m0 = (t / num_n) * BM, n0 = (t % num_n) * BN;
@@ -239,7 +277,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             if (!mbar_wait(&tfull[buf], use & 1, abort_flag, p.status, ERR_WAIT_TMEM_FULL)) break;
             tc_fence_after();
             const uint32_t tbase = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * BN);
-            epilogue_row<BN>(p, tbase, m0 + row_in_tile, n0);
+            epilogue_span(p, tbase, m0 + quad * 32, n0, c0, c1, stage, lane);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tempty[buf]);
@@ -266,9 +304,9 @@ template <int BN> struct Gemm2Cfg {
     static constexpr int A_BYTES = BM * BK * 2;
     static constexpr int B_BYTES = BNH * BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int STAGES_RAW = (SMEM_BUDGET - 2048) / STAGE_BYTES;
+    static constexpr int STAGES_RAW = (SMEM_BUDGET - 2048 - STAGING_BYTES) / STAGE_BYTES;
     static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
-    static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256;
+    static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + STAGING_BYTES + 256;
     static_assert(BN % 16 == 0 && BN >= 32 && BN <= 256, "pair UMMA N must be a multiple of 16 in [32, 256]");
     static_assert(B_BYTES % 1024 == 0, "B stage must keep 1024-byte alignment for the 128B swizzle");
 };
@@ -282,7 +320,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *sA = smem;
     uint8_t *sB = smem + S * Cfg::A_BYTES;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + S * Cfg::STAGE_BYTES);
+    uint8_t *staging = smem + S * Cfg::STAGE_BYTES;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(staging + STAGING_BYTES);
     uint64_t *full = bars, *empty = bars + S, *tfull = bars + 2 * S, *tempty = bars + 2 * S + 2;
     uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 2 * S + 4);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
@@ -297,7 +336,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < S; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 1); }
-        for (int i = 0; i < 2; ++i) { mbar_init(&tfull[i], 1); mbar_init(&tempty[i], 8); }
+        for (int i = 0; i < 2; ++i) { mbar_init(&tfull[i], 1); mbar_init(&tempty[i], 2 * EPI_WARPS); }
         *abort_flag = 0;
         fence_mbar_init();
         prefetch_tensormap(&tmA);
@@ -364,16 +403,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
             }
         }
     } else {
-        const int quad = warp & 3;
+        const int quad = warp & 3, e = warp - 2, half = e >> 2;
+        const int c0 = half ? epi_split<BN>() : 0, c1 = half ? BN : epi_split<BN>();
+        uint8_t *stage = staging + e * (32 * 64);
         int tl = 0;
         for (int t = pair; t < ntiles; t += npairs, ++tl) {
             const int buf = tl & 1;
             const uint32_t use = (uint32_t)(tl >> 1);
             if (!mbar_wait(&tfull[buf], use & 1, abort_flag, p.status, ERR_WAIT_TMEM_FULL)) break;
             tc_fence_after();
-            const int row = (t / num_n) * (2 * BM) + (int)rank * BM + quad * 32 + lane;
+            const int row_base = (t / num_n) * (2 * BM) + (int)rank * BM + quad * 32;
             const uint32_t tbase = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * BN);
-            epilogue_row<BN>(p, tbase, row, (t % num_n) * BN);
+            epilogue_span(p, tbase, row_base, (t % num_n) * BN, c0, c1, stage, lane);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[buf]), 0));

@@ -534,6 +534,27 @@ __global__ void __launch_bounds__(256) k_out128(const bf16 *__restrict__ r2, int
     if (lane == 0) scales[p] = sc;
 }
 
+// ------------------------------------------------------------------ wait probe
+// Waits on an mbarrier that nothing ever arrives on, with a caller-given limit:
+// the bounded-wait path every pipeline kernel relies on. It must end with
+// status ERR_WAIT_PROBE and a usable context, never a trap or a hang.
+__global__ void k_wait_probe(uint64_t limit_ns, int *status) {
+    __shared__ uint64_t bar;
+    __shared__ int abort_flag;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        abort_flag = 0;
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) mbar_wait(&bar, 0, &abort_flag, status, ERR_WAIT_PROBE, limit_ns);
+}
+
+void launch_wait_probe(uint64_t limit_ns, int *status, cudaStream_t st) {
+    k_wait_probe<<<1, 32, 0, st>>>(limit_ns, status);
+    check_launch("k_wait_probe");
+}
+
 // ------------------------------------------------------------------ launchers
 static unsigned blocks_for(int64_t n, int per_block) { return (unsigned)((n + per_block - 1) / per_block); }
 

@@ -66,4 +66,7 @@ void launch_ln_relu2560(__nv_bfloat16 *r, int64_t P, const float *g, const float
 void launch_out128(const __nv_bfloat16 *r2, int64_t P, const uint8_t *empty, float *out, int8_t *codes,
                    float *scales, cudaStream_t st);
 
+// Bounded-wait probe: waits limit_ns on an mbarrier nothing signals, then sets *status.
+void launch_wait_probe(uint64_t limit_ns, int *status, cudaStream_t st);
+
 }  // namespace tcb

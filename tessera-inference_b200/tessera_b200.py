@@ -22,10 +22,11 @@ EXPORTED = [
     "tc_create_multi", "tc_encode_tile", "tc_encode_tile_rows", "tc_encode_tile_device",
     "tc_plan_rows", "tc_set_stream", "tc_set_profiling", "tc_get_stats", "tc_reset_stats",
     "tcb_op_gemm", "tcb_op_count", "tcb_op_gather", "tcb_op_emb1", "tcb_op_attention",
-    "tcb_op_layernorm640", "tcb_op_pool", "tcb_op_ln_relu2560", "tcb_op_out128",
+    "tcb_op_layernorm640", "tcb_op_pool", "tcb_op_ln_relu2560", "tcb_op_out128", "tcb_op_wait_probe",
 ]
 
 CAT_NAMES = ["h2d", "prep", "emb1", "gemm", "attention", "layernorm", "pool", "head", "d2h"]
+GEMM_KINDS = ["emb2", "qkv", "out", "ffn1", "ffn2", "head"]
 
 
 class TcStats(C.Structure):
@@ -33,11 +34,14 @@ class TcStats(C.Structure):
         ("calls", C.c_double), ("pixels", C.c_double), ("tokens", C.c_double),
         ("alg_flop", C.c_double), ("gemm_flop", C.c_double), ("gemm_launches", C.c_double),
         ("launches", C.c_double), ("ms_cat", C.c_double * len(CAT_NAMES)),
+        ("gemm_ms_kind", C.c_double * 6), ("gemm_flop_kind", C.c_double * 6),
     ]
 
     def as_dict(self) -> dict:
-        d = {k: getattr(self, k) for k, _ in self._fields_ if k != "ms_cat"}
+        d = {k: getattr(self, k) for k, _ in self._fields_ if k not in ("ms_cat", "gemm_ms_kind", "gemm_flop_kind")}
         d["ms_cat"] = {n: self.ms_cat[i] for i, n in enumerate(CAT_NAMES)}
+        d["gemm_kind"] = {n: {"ms": self.gemm_ms_kind[i], "flop": self.gemm_flop_kind[i]}
+                          for i, n in enumerate(GEMM_KINDS)}
         return d
 
 
@@ -98,6 +102,8 @@ def load_library(path: os.PathLike | None = None) -> C.CDLL:
     lib.tcb_op_pool.argtypes = [vp, vp, i64, i64, vp, C.c_float, vp, i32, vp]
     lib.tcb_op_ln_relu2560.restype = i32
     lib.tcb_op_ln_relu2560.argtypes = [vp, i64, vp, vp, vp]
+    lib.tcb_op_wait_probe.restype = i32
+    lib.tcb_op_wait_probe.argtypes = [i64, vp, vp]
     lib.tcb_op_out128.restype = i32
     lib.tcb_op_out128.argtypes = [vp, i64, vp, vp, vp, vp, vp]
     if path is None:

@@ -289,3 +289,17 @@ def test_out128_and_quant(lib):
     np.testing.assert_array_equal(codes.cpu().numpy(), qc)
     np.testing.assert_array_equal(scales.cpu().numpy().view(np.uint32), qs.view(np.uint32))
     assert np.all(scales.cpu().numpy()[::97] == np.float32(1e-12) / np.float32(127.0))
+
+
+def test_bounded_wait_reports_status(lib):
+    """A wait that nothing will ever satisfy ends after its limit with an error
+    status instead of a hang; the context remains usable afterwards."""
+    import time
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    t0 = time.perf_counter()
+    assert lib.tcb_op_wait_probe(1000, _p(status), _stream()) == 0  # 1 ms limit
+    torch.cuda.synchronize()
+    assert time.perf_counter() - t0 < 5.0
+    assert status.item() == 6
+    x = torch.ones(4, device="cuda")
+    assert float((x * 2).sum()) == 8.0  # context still healthy
