@@ -26,6 +26,13 @@ int tcb_op_gemm(const void *A, int lda, const void *W, const float *bias, int re
                 const float *pe_doy, int pe_stride, const void *pe_table, const float *pe_div, void *out, int ldo,
                 int M, int N, int K, int bn, int variant, int *status, void *stream);
 
+/* out[M,640] = bf16(LayerNorm(y) * ln_g + ln_b), y = bf16(A[M,K] W[640,K]^T + bias + res),
+ * LayerNorm eps 1e-5 over the 640 columns: the reference's out-proj + LN1 and
+ * FFN2 + LN2 (src/tessera_cpu.cpp:424-428, 245-263) fused into one GEMM whose
+ * epilogue exchanges row statistics across a 4-CTA cluster. */
+int tcb_op_gemm_ln(const void *A, int lda, const void *W, const float *bias, const void *res, int ldr,
+                   const float *ln_g, const float *ln_b, void *out, int ldo, int M, int K, int *status, void *stream);
+
 /* Valid-observation counts (src/tessera_encode.cpp:245-257) of pixels [p0, p0+np). */
 int tcb_op_count(const uint8_t *masks, const int16_t *asc, const int16_t *desc, int64_t T2, int64_t Ta, int64_t Td,
                  int64_t N, int64_t p0, int64_t np, int32_t *n2, int32_t *n1, void *stream);

@@ -331,7 +331,8 @@ static void dev_init(Dev &d, int device, const Blob &blob, const ModelOff &off) 
 enum GemmKind { GK_EMB2 = 0, GK_QKV, GK_OUT, GK_FFN1, GK_FFN2, GK_HEAD };
 
 static void gemm(Dev &d, int kind, const Lin &L, const bf16 *A, int64_t M, bf16 *out, bool relu,
-                 const bf16 *res = nullptr, const float *pe_doy = nullptr, int pe_stride = 1) {
+                 const bf16 *res = nullptr, const float *pe_doy = nullptr, int pe_stride = 1,
+                 const float *ln_g = nullptr, const float *ln_b = nullptr) {
     if (M <= 0) return;
     d.mark(100 + kind);
     GemmArgs p;
@@ -349,11 +350,25 @@ static void gemm(Dev &d, int kind, const Lin &L, const bf16 *A, int64_t M, bf16 
     p.out = out;
     p.ldo = L.N;
     p.status = d.status.p;
+    p.ln_g = ln_g;
+    p.ln_b = ln_b;
     launch_gemm(p, A, L.K, L.w, d.st);
     d.stats.gemm_flop += 2.0 * double(M) * L.N * L.K;
     d.stats.gemm_flop_kind[kind] += 2.0 * double(M) * L.N * L.K;
     d.stats.gemm_launches += 1;
     d.stats.launches += 1;
+}
+
+// TC_LN_FUSE=1 runs LN1 / LN2 in the epilogues of out-proj / FFN2 (4-CTA
+// cluster exchanging row statistics) instead of as a separate kernel. Off by
+// default: on config 1 the fused GEMMs lost more time (out-proj + FFN2
+// 2.80 s -> 5.05 s per tile) than the LayerNorm kernel they replace (1.12 s).
+static bool ln_fused() {
+    static const bool on = [] {
+        const char *e = std::getenv("TC_LN_FUSE");
+        return e && *e == '1';
+    }();
+    return on;
 }
 
 // One backbone over a chunk's token stream: records (M, C+1) -> fused[:, col0:col0+640].
@@ -369,14 +384,21 @@ static void backbone(Dev &d, int b, const float *rec, Segs segs, int64_t M, int 
             gemm(d, GK_QKV, B.qkv[l], d.x.p, M, d.qkv.p, false);
             d.mark(TC_CAT_ATTN);
             launch_attention(d.qkv.p, segs, npix, Tmax, d.att.p, d.st);
-            gemm(d, GK_OUT, B.out[l], d.att.p, M, d.y.p, false, d.x.p);
-            d.mark(TC_CAT_LN);
-            launch_layernorm640(d.y.p, M, B.ln1g[l], B.ln1b[l], d.x1.p, d.st);
-            gemm(d, GK_FFN1, B.ffn1[l], d.x1.p, M, d.hbuf.p, true);
-            gemm(d, GK_FFN2, B.ffn2[l], d.hbuf.p, M, d.y.p, false, d.x1.p);
-            d.mark(TC_CAT_LN);
-            launch_layernorm640(d.y.p, M, B.ln2g[l], B.ln2b[l], d.x.p, d.st);
-            d.stats.launches += 3;
+            if (ln_fused()) {  // LN1 / LN2 in the epilogues of out-proj / FFN2
+                gemm(d, GK_OUT, B.out[l], d.att.p, M, d.x1.p, false, d.x.p, nullptr, 1, B.ln1g[l], B.ln1b[l]);
+                gemm(d, GK_FFN1, B.ffn1[l], d.x1.p, M, d.hbuf.p, true);
+                gemm(d, GK_FFN2, B.ffn2[l], d.hbuf.p, M, d.x.p, false, d.x1.p, nullptr, 1, B.ln2g[l], B.ln2b[l]);
+                d.stats.launches += 1;
+            } else {
+                gemm(d, GK_OUT, B.out[l], d.att.p, M, d.y.p, false, d.x.p);
+                d.mark(TC_CAT_LN);
+                launch_layernorm640(d.y.p, M, B.ln1g[l], B.ln1b[l], d.x1.p, d.st);
+                gemm(d, GK_FFN1, B.ffn1[l], d.x1.p, M, d.hbuf.p, true);
+                gemm(d, GK_FFN2, B.ffn2[l], d.hbuf.p, M, d.y.p, false, d.x1.p);
+                d.mark(TC_CAT_LN);
+                launch_layernorm640(d.y.p, M, B.ln2g[l], B.ln2b[l], d.x.p, d.st);
+                d.stats.launches += 3;
+            }
         }
     }
     d.mark(TC_CAT_POOL);
@@ -894,6 +916,19 @@ int tcb_op_gemm(const void *A, int lda, const void *W, const float *bias, int re
         p.out = static_cast<bf16 *>(out); p.ldo = ldo; p.status = status;
         launch_gemm(p, static_cast<const bf16 *>(A), lda, static_cast<const bf16 *>(W),
                     static_cast<cudaStream_t>(stream), bn, 0, variant);
+    })
+}
+
+int tcb_op_gemm_ln(const void *A, int lda, const void *W, const float *bias, const void *res, int ldr,
+                   const float *ln_g, const float *ln_b, void *out, int ldo, int M, int K, int *status, void *stream) {
+    OP_TRY("tcb_op_gemm_ln", {
+        GemmArgs p;
+        p.M = M; p.N = 640; p.K = K; p.bias = bias;
+        p.res = static_cast<const bf16 *>(res); p.ldr = ldr;
+        p.out = static_cast<bf16 *>(out); p.ldo = ldo; p.status = status;
+        p.ln_g = ln_g; p.ln_b = ln_b;
+        launch_gemm(p, static_cast<const bf16 *>(A), lda, static_cast<const bf16 *>(W),
+                    static_cast<cudaStream_t>(stream));
     })
 }
 

@@ -64,7 +64,7 @@ __device__ __forceinline__ float pe_value(float doy, int n, const bf16 *__restri
 // columns of one output row, packed into two 16-byte words.
 __device__ __forceinline__ void epilogue_cols16(const GemmArgs &p, const uint32_t (&r)[16], const uint4 (&res)[2],
                                                 bool has_res, float pe_doy, bool pe_tab, int pe_di, int n,
-                                                uint4 (&o)[2]) {
+                                                uint4 (&o)[2], bool pe_irregular) {
     float v[16];
 #pragma unroll
     for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
@@ -90,7 +90,7 @@ __device__ __forceinline__ void epilogue_cols16(const GemmArgs &p, const uint32_
                 v[8 * h + 2 * j + 1] += bf16hi(w[j]);
             }
         }
-    } else if (p.pe_doy) {
+    } else if (pe_irregular) {  // a day of year outside the table: sinusoid computed per element
 #pragma unroll
         for (int j = 0; j < 16; ++j) v[j] += pe_value(pe_doy, n + j, p.pe_table, p.pe_div, pe_tab, pe_di);
     }
@@ -105,47 +105,57 @@ __device__ __forceinline__ void epilogue_cols16(const GemmArgs &p, const uint32_
 // first output column is n0. Per group of 32 columns: TMEM -> registers ->
 // epilogue math -> a 2 KB staging buffer (32 rows x 64 B, 16-byte chunks XOR-
 // swizzled so both the row-wise writes and the read-back are conflict-free) ->
-// row-contiguous 64-byte global stores, 8 rows per instruction. Residual loads
-// for a group are issued before its TMEM wait.
-__device__ __forceinline__ void epilogue_span(const GemmArgs &p, uint32_t tbase, int row_base, int n0, int c0, int c1,
-                                              uint8_t *stage, int lane) {
+// row-contiguous 64-byte global stores, 8 rows per instruction.
+// The residual (or, for an integer day of year, the DOY-table row, which is
+// an ordinary residual row) is software-pipelined one group ahead, and the
+// first group's loads are issued before waiting for the accumulator.
+// Returns false if the wait for the accumulator gave up.
+__device__ __forceinline__ bool epilogue_tile(const GemmArgs &p, uint32_t tbase, int row_base, int n0, int c0, int c1,
+                                              uint8_t *stage, int lane, uint64_t *tfull_bar, uint32_t parity,
+                                              volatile int *abort_flag) {
     const int row = row_base + lane;
     const bool live = row < p.M;
     const bf16 *res_row = nullptr;
-    bool pe_tab = false;
-    int pe_di = 0;
+    bool pe_irregular = false;
     float pe_doy = 0.f;
     if (live) {
-        if (p.res) res_row = p.res + (size_t)row * p.ldr;
-        if (p.pe_doy) {
+        if (p.res) {
+            res_row = p.res + (size_t)row * p.ldr;
+        } else if (p.pe_doy) {
             pe_doy = p.pe_doy[(size_t)row * p.pe_stride];
-            if (pe_doy >= 0.f && pe_doy <= 366.f && floorf(pe_doy) == pe_doy) {
-                pe_tab = true;
-                pe_di = (int)pe_doy;
-            }
+            if (pe_doy >= 0.f && pe_doy <= 366.f && floorf(pe_doy) == pe_doy) res_row = p.pe_table + (int)pe_doy * D;
+            else pe_irregular = true;
         }
     }
+    uint4 qn[4] = {};
+    auto load_group = [&](int c, uint4 (&q)[4]) {
+        if (res_row) {
+            const uint4 *r4 = reinterpret_cast<const uint4 *>(res_row + n0 + c);
+            q[0] = r4[0];
+            q[1] = r4[1];
+            if (c + 32 <= c1) { q[2] = r4[2]; q[3] = r4[3]; }
+        }
+    };
+    load_group(c0, qn);
+    if (!mbar_wait(tfull_bar, parity, abort_flag, p.status, ERR_WAIT_TMEM_FULL)) return false;
+    tc_fence_after();
     uint4 *my_row = reinterpret_cast<uint4 *>(stage + lane * 64);
     const int sw = (lane >> 1) & 3;
 #pragma unroll 1
     for (int c = c0; c < c1; c += 32) {
         const bool two = c + 32 <= c1;
+        const uint4 q0[2] = {qn[0], qn[1]}, q1[2] = {qn[2], qn[3]};
+        if (c + 32 < c1) load_group(c + 32, qn);
         uint32_t r0[16], r1[16];
-        uint4 q0[2] = {}, q1[2] = {};
-        if (res_row) {
-            const uint4 *r4 = reinterpret_cast<const uint4 *>(res_row + n0 + c);
-            q0[0] = r4[0]; q0[1] = r4[1];
-            if (two) { q1[0] = r4[2]; q1[1] = r4[3]; }
-        }
         tmem_ld16(tbase + (uint32_t)c, r0);
         if (two) tmem_ld16(tbase + (uint32_t)(c + 16), r1);
         tmem_ld_wait();
         uint4 o[2];
-        epilogue_cols16(p, r0, q0, res_row != nullptr, pe_doy, pe_tab, pe_di, n0 + c, o);
+        epilogue_cols16(p, r0, q0, res_row != nullptr, pe_doy, false, 0, n0 + c, o, pe_irregular);
         my_row[0 ^ sw] = o[0];
         my_row[1 ^ sw] = o[1];
         if (two) {
-            epilogue_cols16(p, r1, q1, res_row != nullptr, pe_doy, pe_tab, pe_di, n0 + c + 16, o);
+            epilogue_cols16(p, r1, q1, res_row != nullptr, pe_doy, false, 0, n0 + c + 16, o, pe_irregular);
             my_row[2 ^ sw] = o[0];
             my_row[3 ^ sw] = o[1];
         }
@@ -169,6 +179,7 @@ __device__ __forceinline__ void epilogue_span(const GemmArgs &p, uint32_t tbase,
         }
         __syncwarp();
     }
+    return true;
 }
 
 // Column split of a BN-wide tile between the two epilogue warps of a quadrant
@@ -274,10 +285,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             const int m0 = (t / num_n) * BM, n0 = (t % num_n) * BN;
             const int buf = tl & 1;
             const uint32_t use = (uint32_t)(tl >> 1);
-            if (!mbar_wait(&tfull[buf], use & 1, abort_flag, p.status, ERR_WAIT_TMEM_FULL)) break;
-            tc_fence_after();
             const uint32_t tbase = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * BN);
-            epilogue_span(p, tbase, m0 + quad * 32, n0, c0, c1, stage, lane);
+            if (!epilogue_tile(p, tbase, m0 + quad * 32, n0, c0, c1, stage, lane, &tfull[buf], use & 1, abort_flag))
+                break;
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tempty[buf]);
@@ -410,11 +420,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
         for (int t = pair; t < ntiles; t += npairs, ++tl) {
             const int buf = tl & 1;
             const uint32_t use = (uint32_t)(tl >> 1);
-            if (!mbar_wait(&tfull[buf], use & 1, abort_flag, p.status, ERR_WAIT_TMEM_FULL)) break;
-            tc_fence_after();
             const int row_base = (t / num_n) * (2 * BM) + (int)rank * BM + quad * 32;
             const uint32_t tbase = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * BN);
-            epilogue_span(p, tbase, row_base, (t % num_n) * BN, c0, c1, stage, lane);
+            if (!epilogue_tile(p, tbase, row_base, (t % num_n) * BN, c0, c1, stage, lane, &tfull[buf], use & 1,
+                               abort_flag))
+                break;
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[buf]), 0));
@@ -426,6 +436,314 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
     cluster_sync();  // no CTA leaves while its peer may still signal its barriers or use its TMEM
     tc_fence_after();
     if (warp == 1) tmem_dealloc_pair(tmem_base, 512);
+}
+
+// ------------------------------------------------------------------ LayerNorm-fused variant (N = 640)
+// A cluster of four CTAs owns one 128-row block of the 640-column output;
+// cluster rank r computes columns [160 r, 160 r + 160) with the single-CTA
+// pipeline. The epilogue never writes y:
+//   pass A  y = bf16(acc + bias [+ residual]) per 32-column group; the row's
+//           count / mean / M2 over the warp's columns, merged group by group
+//           with Chan's parallel-variance update;
+//   exchange  each of the 8 epilogue warps x 4 CTAs stores (mean, M2) of its
+//           rows into every cluster CTA's shared memory (st.shared::cluster),
+//           then arrives on each CTA's exchange barrier (release.cluster);
+//           after its own barrier completes (acquire.cluster) a CTA merges the
+//           8 partials of each row in a fixed order: mean and variance of all
+//           640 values (biased, as the reference LayerNorm);
+//   pass B  y recomputed from TMEM, out = bf16((y - mean) rstd g + b), staged
+//           through shared memory and stored row-contiguously.
+// This is LN1 fused into out-proj and LN2 into FFN2 (tessera_cpu.cpp:424-428).
+constexpr int LN_N = 640, LN_BN = 160, LN_CTAS = 4;
+constexpr int LN_CONTRIB = 2 * LN_CTAS;                  // epilogue warps covering one row
+constexpr int XCH_BYTES = 2 * LN_CONTRIB * BM * 8;       // [tile parity][contributor][row] (mean, M2)
+struct GemmLnCfg {
+    static constexpr int A_BYTES = BM * BK * 2;
+    static constexpr int B_BYTES = LN_BN * BK * 2;
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int STAGES_RAW = (SMEM_BUDGET - 2048 - STAGING_BYTES - XCH_BYTES) / STAGE_BYTES;
+    static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
+    static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + STAGING_BYTES + XCH_BYTES + 256;
+};
+
+// y values of one 16-column group, rounded to bf16 (the value the reference
+// hands to LayerNorm), as floats.
+__device__ __forceinline__ void ln_y16(const GemmArgs &p, const uint32_t (&r)[16], const uint4 (&res)[2], bool has_res,
+                                       int n, float (&y)[16]) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) y[j] = __uint_as_float(r[j]);
+    if (p.bias) {
+        const float4 *b4 = reinterpret_cast<const float4 *>(p.bias + n);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float4 b = __ldg(b4 + j);
+            y[4 * j] += b.x; y[4 * j + 1] += b.y; y[4 * j + 2] += b.z; y[4 * j + 3] += b.w;
+        }
+    }
+    if (p.relu) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) y[j] = fmaxf(y[j], 0.f);
+    }
+    if (has_res) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const uint32_t w[4] = {res[h].x, res[h].y, res[h].z, res[h].w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                y[8 * h + 2 * j] += bf16lo(w[j]);
+                y[8 * h + 2 * j + 1] += bf16hi(w[j]);
+            }
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < 16; ++j) y[j] = bf16_round(y[j]);
+}
+
+// Chan et al. merge of (n_b, mean_b, m2_b) into (n, mean, m2).
+__device__ __forceinline__ void chan_merge(float &n, float &mean, float &m2, float nb, float meanb, float m2b) {
+    const float tot = n + nb;
+    const float delta = meanb - mean;
+    mean += delta * (nb / tot);
+    m2 += m2b + delta * delta * (n * nb / tot);
+    n = tot;
+}
+
+__device__ __forceinline__ bool ln_epilogue_tile(const GemmArgs &p, uint32_t tbase, int row_base, int n0, int c0,
+                                                 int c1, uint8_t *stage, int lane, uint64_t *tfull_bar,
+                                                 uint32_t tfull_parity, float2 *xch, uint64_t *xbar,
+                                                 uint32_t xbar_parity, int contributor, int quad,
+                                                 volatile int *abort_flag) {
+    const int row = row_base + lane;
+    const bool live = row < p.M;
+    const bf16 *res_row = (live && p.res) ? p.res + (size_t)row * p.ldr : nullptr;
+    auto load_group = [&](int c, uint4 (&q)[4]) {
+        if (res_row) {
+            const uint4 *r4 = reinterpret_cast<const uint4 *>(res_row + n0 + c);
+            q[0] = r4[0];
+            q[1] = r4[1];
+            if (c + 32 <= c1) { q[2] = r4[2]; q[3] = r4[3]; }
+        }
+    };
+    uint4 qn[4] = {};
+    load_group(c0, qn);
+    if (!mbar_wait(tfull_bar, tfull_parity, abort_flag, p.status, ERR_WAIT_TMEM_FULL)) return false;
+    tc_fence_after();
+    // ---- pass A: statistics of this warp's columns
+    float cnt = 0.f, mean = 0.f, m2 = 0.f;
+#pragma unroll 1
+    for (int c = c0; c < c1; c += 32) {
+        const bool two = c + 32 <= c1;
+        const uint4 q0[2] = {qn[0], qn[1]}, q1[2] = {qn[2], qn[3]};
+        if (c + 32 < c1) load_group(c + 32, qn);
+        uint32_t r0[16], r1[16];
+        tmem_ld16(tbase + (uint32_t)c, r0);
+        if (two) tmem_ld16(tbase + (uint32_t)(c + 16), r1);
+        tmem_ld_wait();
+        float y[16];
+        ln_y16(p, r0, q0, res_row != nullptr, n0 + c, y);
+        float s = 0.f;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) s += y[j];
+        float gm = s / 16.f, g2 = 0.f;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) { const float d = y[j] - gm; g2 += d * d; }
+        chan_merge(cnt, mean, m2, 16.f, gm, g2);
+        if (two) {
+            ln_y16(p, r1, q1, res_row != nullptr, n0 + c + 16, y);
+            s = 0.f;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) s += y[j];
+            gm = s / 16.f;
+            g2 = 0.f;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) { const float d = y[j] - gm; g2 += d * d; }
+            chan_merge(cnt, mean, m2, 16.f, gm, g2);
+        }
+    }
+    // ---- exchange (mean, M2) of this warp's rows with the 4 cluster CTAs
+    const int rloc = quad * 32 + lane;
+    const uint32_t slot = smem_u32(&xch[contributor * BM + rloc]);
+#pragma unroll
+    for (int dst = 0; dst < LN_CTAS; ++dst) st_cluster_f32x2(mapa_shared(slot, (uint32_t)dst), mean, m2);
+    fence_acq_rel_cluster();
+    __syncwarp();
+    if (lane == 0) {
+#pragma unroll
+        for (int dst = 0; dst < LN_CTAS; ++dst) mbar_arrive_cluster(mapa_shared(smem_u32(xbar), (uint32_t)dst));
+    }
+    if (!mbar_wait_cluster(xbar, xbar_parity, abort_flag, p.status, ERR_WAIT_LN_EXCHANGE)) return false;
+    float n_all = 0.f, mean_all = 0.f, m2_all = 0.f;
+#pragma unroll
+    for (int k = 0; k < LN_CONTRIB; ++k) {
+        const float2 v = xch[k * BM + rloc];
+        const float nk = (k & 1) ? float(LN_BN - epi_split<LN_BN>()) : float(epi_split<LN_BN>());
+        chan_merge(n_all, mean_all, m2_all, nk, v.x, v.y);
+    }
+    const float rstd = 1.f / sqrtf(m2_all / (float)LN_N + LN_EPS);
+    // ---- pass B: normalise and store
+    load_group(c0, qn);
+    uint4 *my_row = reinterpret_cast<uint4 *>(stage + lane * 64);
+    const int sw = (lane >> 1) & 3;
+#pragma unroll 1
+    for (int c = c0; c < c1; c += 32) {
+        const bool two = c + 32 <= c1;
+        const uint4 q0[2] = {qn[0], qn[1]}, q1[2] = {qn[2], qn[3]};
+        if (c + 32 < c1) load_group(c + 32, qn);
+        uint32_t r0[16], r1[16];
+        tmem_ld16(tbase + (uint32_t)c, r0);
+        if (two) tmem_ld16(tbase + (uint32_t)(c + 16), r1);
+        tmem_ld_wait();
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            if (h == 1 && !two) break;
+            float y[16];
+            const int n = n0 + c + 16 * h;
+            ln_y16(p, h ? r1 : r0, h ? q1 : q0, res_row != nullptr, n, y);
+            float o[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) o[j] = (y[j] - mean_all) * rstd * __ldg(p.ln_g + n + j) + __ldg(p.ln_b + n + j);
+            my_row[(2 * h) ^ sw] = make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]),
+                                              pack_bf16x2(o[4], o[5]), pack_bf16x2(o[6], o[7]));
+            my_row[(2 * h + 1) ^ sw] = make_uint4(pack_bf16x2(o[8], o[9]), pack_bf16x2(o[10], o[11]),
+                                                  pack_bf16x2(o[12], o[13]), pack_bf16x2(o[14], o[15]));
+        }
+        __syncwarp();
+        if (two) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int rr = i * 8 + (lane >> 2), k = lane & 3;
+                const uint4 v = reinterpret_cast<const uint4 *>(stage + rr * 64)[k ^ ((rr >> 1) & 3)];
+                if (row_base + rr < p.M)
+                    *reinterpret_cast<uint4 *>(p.out + (size_t)(row_base + rr) * p.ldo + n0 + c + k * 8) = v;
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+                const int rr = i * 16 + (lane >> 1), k = lane & 1;
+                const uint4 v = reinterpret_cast<const uint4 *>(stage + rr * 64)[k ^ ((rr >> 1) & 3)];
+                if (row_base + rr < p.M)
+                    *reinterpret_cast<uint4 *>(p.out + (size_t)(row_base + rr) * p.ldo + n0 + c + k * 8) = v;
+            }
+        }
+        __syncwarp();
+    }
+    return true;
+}
+
+__global__ void __cluster_dims__(LN_CTAS, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
+    k_gemm_ln640(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs p) {
+    using Cfg = GemmLnCfg;
+    constexpr int S = Cfg::STAGES;
+    constexpr int BN = LN_BN;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *sA = smem;
+    uint8_t *sB = smem + S * Cfg::A_BYTES;
+    uint8_t *staging = smem + S * Cfg::STAGE_BYTES;
+    float2 *xch = reinterpret_cast<float2 *>(staging + STAGING_BYTES);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(staging + STAGING_BYTES + XCH_BYTES);
+    uint64_t *full = bars, *empty = bars + S, *tfull = bars + 2 * S, *tempty = bars + 2 * S + 2;
+    uint64_t *xbar = bars + 2 * S + 4;
+    uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 2 * S + 6);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const int cl = blockIdx.x / LN_CTAS, ncl = gridDim.x / LN_CTAS;
+    const int num_m = (p.M + BM - 1) / BM;
+    const int nk = p.K / BK;
+    const int n0 = (int)rank * BN;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < S; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 1); }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&tfull[i], 1);
+            mbar_init(&tempty[i], EPI_WARPS);
+            mbar_init(&xbar[i], EPI_WARPS * LN_CTAS);
+        }
+        *abort_flag = 0;
+        fence_mbar_init();
+        prefetch_tensormap(&tmA);
+        prefetch_tensormap(&tmB);
+    }
+    if (warp == 1) { tmem_alloc(tmem_holder, 512); tmem_relinquish(); }
+    tc_fence_before();
+    cluster_sync();  // every CTA's exchange barriers exist before any remote arrival
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_holder;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int s = 0;
+            uint32_t ph = 0;
+            for (int mb = cl; mb < num_m; mb += ncl) {
+                bool ok = true;
+                for (int kb = 0; kb < nk; ++kb) {
+                    if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, p.status, ERR_WAIT_SMEM_EMPTY)) { ok = false; break; }
+                    mbar_arrive_expect_tx(&full[s], Cfg::STAGE_BYTES);
+                    tma_load_2d(sA + s * Cfg::A_BYTES, &tmA, kb * BK, mb * BM, &full[s]);
+                    tma_load_2d(sB + s * Cfg::B_BYTES, &tmB, kb * BK, n0, &full[s]);
+                    if (++s == S) { s = 0; ph ^= 1; }
+                }
+                if (!ok) break;
+            }
+            for (int i = 0; i < S; ++i) {
+                if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, p.status, ERR_WAIT_SMEM_EMPTY)) break;
+                if (++s == S) { s = 0; ph ^= 1; }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = umma_idesc_bf16(BM, BN);
+            int s = 0;
+            uint32_t ph = 0;
+            int tl = 0;
+            for (int mb = cl; mb < num_m; mb += ncl, ++tl) {
+                const int buf = tl & 1;
+                const uint32_t use = (uint32_t)(tl >> 1);
+                if (!mbar_wait(&tempty[buf], (use & 1) ^ 1, abort_flag, p.status, ERR_WAIT_TMEM_EMPTY)) break;
+                tc_fence_after();
+                const uint32_t d = tmem_base + (uint32_t)(buf * BN);
+                bool ok = true;
+                for (int kb = 0; kb < nk; ++kb) {
+                    if (!mbar_wait(&full[s], ph, abort_flag, p.status, ERR_WAIT_TMA_FULL)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint64_t adesc = umma_desc_sw128(smem_u32(sA + s * Cfg::A_BYTES));
+                    const uint64_t bdesc = umma_desc_sw128(smem_u32(sB + s * Cfg::B_BYTES));
+#pragma unroll
+                    for (int k = 0; k < BK / UMMA_K; ++k)
+                        umma_bf16(d, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), idesc, (kb | k) != 0 ? 1u : 0u);
+                    umma_commit(&empty[s]);
+                    if (++s == S) { s = 0; ph ^= 1; }
+                }
+                if (!ok) break;
+                umma_commit(&tfull[buf]);
+            }
+        }
+    } else {
+        const int quad = warp & 3, e = warp - 2, half = e >> 2;
+        const int c0 = half ? epi_split<BN>() : 0, c1 = half ? BN : epi_split<BN>();
+        uint8_t *stage = staging + e * (32 * 64);
+        const int contributor = (int)rank * 2 + half;
+        int tl = 0;
+        for (int mb = cl; mb < num_m; mb += ncl, ++tl) {
+            const int buf = tl & 1;
+            const uint32_t use = (uint32_t)(tl >> 1);
+            const uint32_t tbase = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * BN);
+            if (!ln_epilogue_tile(p, tbase, mb * BM + quad * 32, n0, c0, c1, stage, lane, &tfull[buf], use & 1,
+                                  xch + buf * LN_CONTRIB * BM, &xbar[buf], use & 1, contributor, quad, abort_flag))
+                break;
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[buf]);
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();  // no CTA leaves while a peer may still write its exchange slots or barriers
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc(tmem_base, 512);
 }
 
 // ------------------------------------------------------------------ host side
@@ -515,6 +833,31 @@ template <int BN> static void launch_pair(const GemmArgs &p, const bf16 *A, int 
     k_gemm2_bf16<BN><<<2 * pairs, GEMM_THREADS, Cfg::SMEM_BYTES, st>>>(ta, tb, p);
 }
 
+static void launch_ln(const GemmArgs &p, const bf16 *A, int lda, const bf16 *W, cudaStream_t st) {
+    using Cfg = GemmLnCfg;
+    static int max_clusters[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!max_clusters[dev & 63]) {
+        cudaError_t e = cudaFuncSetAttribute(k_gemm_ln640, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
+        if (e != cudaSuccess) throw std::runtime_error(std::string("gemm_ln smem attribute: ") + cudaGetErrorString(e));
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(LN_CTAS * 64);
+        cfg.blockDim = dim3(GEMM_THREADS);
+        cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
+        int n = 0;
+        e = cudaOccupancyMaxActiveClusters(&n, k_gemm_ln640, &cfg);
+        if (e != cudaSuccess || n <= 0) throw std::runtime_error("gemm_ln: no cluster of 4 fits on this device");
+        max_clusters[dev & 63] = n;
+    }
+    CUtensorMap ta, tb;
+    make_tmap(&ta, A, (uint64_t)p.M, (uint64_t)p.K, (uint64_t)lda, BM);
+    make_tmap(&tb, W, (uint64_t)LN_N, (uint64_t)p.K, (uint64_t)p.K, LN_BN);
+    const int num_m = (p.M + BM - 1) / BM;
+    const int clusters = std::max(1, std::min(num_m, max_clusters[dev & 63]));
+    k_gemm_ln640<<<LN_CTAS * clusters, GEMM_THREADS, Cfg::SMEM_BYTES, st>>>(ta, tb, p);
+}
+
 // TC_GEMM_VARIANT=1 forces the single-CTA kernel, 2 the CTA-pair kernel.
 int gemm_default_variant() {
     static int v = [] {
@@ -539,6 +882,11 @@ void launch_gemm(const GemmArgs &p, const bf16 *A, int lda, const bf16 *W, cudaS
     if (bn == 0) bn = gemm_pick_bn(p.N);
     if (bn == 0 || p.N % bn) throw std::runtime_error("gemm: unsupported N " + std::to_string(p.N));
     if (p.ldo % 8 || (p.res && p.ldr % 8)) throw std::runtime_error("gemm: output/residual pitch must be 16-byte aligned");
+    if (p.ln_g) {
+        if (p.N != LN_N || !p.ln_b || p.pe_doy) throw std::runtime_error("gemm: LayerNorm epilogue needs N = 640");
+        launch_ln(p, A, lda, W, st);
+        return;
+    }
     if (variant == 0) variant = gemm_default_variant();
     if (variant == 2) {
         switch (bn) {

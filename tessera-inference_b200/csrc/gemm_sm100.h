@@ -24,6 +24,11 @@ struct GemmArgs {
     __nv_bfloat16 *out = nullptr;
     int ldo = 0;
     int *status = nullptr;  // device status word (0 = ok)
+    // When set (N = 640 only): out = bf16(LayerNorm(y) * ln_g + ln_b) of the
+    // bf16-rounded y = [relu](A W^T + bias) + residual, eps 1e-5, fused in the
+    // epilogue of a 4-CTA cluster (one 160-column tile per CTA).
+    const float *ln_g = nullptr;
+    const float *ln_b = nullptr;
 };
 
 // Tile width BN used for a given N (0 = unsupported).
