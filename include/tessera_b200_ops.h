@@ -33,6 +33,19 @@ int tcb_op_gemm(const void *A, int lda, const void *W, const float *bias, int re
 int tcb_op_gemm_ln(const void *A, int lda, const void *W, const float *bias, const void *res, int ldr,
                    const float *ln_g, const float *ln_b, void *out, int ldo, int M, int K, int *status, void *stream);
 
+/* Allocation-free form of tcb_op_gemm_ln, with no counterpart in the
+ * reference. For callers that may not allocate device memory, such as a plugin
+ * whose host framework owns the whole device-memory budget, or a hot path
+ * where cudaMalloc could fail or would synchronise the device: the caller
+ * passes inputs and the output only (out has pitch 640), and the intermediate
+ * rows and status word live in a fixed 10 MiB static device array that every
+ * GPU loading this library holds until exit. M is at most 8192 (larger M
+ * returns -1 with a message). The first call on a device looks up the array's
+ * address, so make it before any stream capture. Calls share the array: two
+ * calls that overlap on the GPU race. Returns after the work completes. */
+int tcb_op_gemm_ln_noalloc(const void *A, int lda, const void *W, const float *bias, const void *res, int ldr,
+                           const float *ln_g, const float *ln_b, void *out, int M, int K, void *stream);
+
 /* Valid-observation counts (src/tessera_encode.cpp:245-257) of pixels [p0, p0+np). */
 int tcb_op_count(const uint8_t *masks, const int16_t *asc, const int16_t *desc, int64_t T2, int64_t Ta, int64_t Td,
                  int64_t N, int64_t p0, int64_t np, int32_t *n2, int32_t *n1, void *stream);
