@@ -12,8 +12,9 @@
 //   warp 0      TMA producer: A and W tiles (128-byte swizzle) into a ring of
 //               shared-memory stages, completion tracked by mbarriers.
 //   warp 1      TMEM allocator and MMA issuer: one elected thread issues
-//               tcgen05.mma (M=128, N=BN, K=16) into a double-buffered f32
-//               accumulator in tensor memory and commits stage/tile barriers.
+//               tcgen05.mma (M=128, N=BN, K=16; the last column tile may be
+//               narrower) into a double-buffered f32 accumulator in tensor
+//               memory and commits stage/tile barriers.
 //   warps 2-9   epilogue: tcgen05.ld of the accumulator (two warps per TMEM
 //               lane quadrant, splitting the columns; one output row per
 //               lane), bias, ReLU, residual, bf16 rounding, then a swizzled
@@ -182,13 +183,21 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs &p, uint32_t tbase,
     return true;
 }
 
-// Column split of a BN-wide tile between the two epilogue warps of a quadrant
+// Column split of a w-wide tile between the two epilogue warps of a quadrant
 // (at a multiple of 32 near the middle).
-template <int BN> __host__ __device__ constexpr int epi_split() { return ((BN / 2 + 16) / 32) * 32; }
+__host__ __device__ constexpr int epi_split(int w) { return ((w / 2 + 16) / 32) * 32; }
+template <int BN> __host__ __device__ constexpr int epi_split() { return epi_split(BN); }
 
+// N is covered by ceil(N / BN) column tiles: all BN wide except the last,
+// which is `tail` = N - (num_n - 1) * BN wide (a multiple of 16) and has its own
+// tensor map (tmBt, box rows = tail) and UMMA instruction descriptor. With
+// BN = 256 this keeps every MMA but the tail's at the full N = 256 issue width
+// (N = 640 -> 256, 256, 128), which runs faster than equal narrower tiles:
+// an M = 128, K = 16 MMA takes about as long at N = 128 or 160 as at N = 256.
 template <int BN>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
-    k_gemm_bf16(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs p) {
+    k_gemm_bf16(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                const __grid_constant__ CUtensorMap tmBt, GemmArgs p) {
     using Cfg = GemmCfg<BN>;
     constexpr int S = Cfg::STAGES;
     extern __shared__ uint8_t smem_raw[];
@@ -202,7 +211,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int num_n = p.N / BN;
+    const int num_n = (p.N + BN - 1) / BN;
+    const int tail = p.N - (num_n - 1) * BN;
     const int num_m = (p.M + BM - 1) / BM;
     const int ntiles = num_m * num_n;
     const int nk = p.K / BK;
@@ -214,6 +224,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         fence_mbar_init();
         prefetch_tensormap(&tmA);
         prefetch_tensormap(&tmB);
+        if (tail != BN) prefetch_tensormap(&tmBt);
     }
     if (warp == 1) { tmem_alloc(tmem_holder, 512); tmem_relinquish(); }
     tc_fence_before();
@@ -226,13 +237,16 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             int s = 0;
             uint32_t ph = 0;
             for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
-                const int m0 = (t / num_n) * BM, n0 = (t % num_n) * BN;
+                const int nt = t % num_n, m0 = (t / num_n) * BM, n0 = nt * BN;
+                const bool last = nt == num_n - 1;
+                const CUtensorMap *tb = last ? &tmBt : &tmB;
+                const uint32_t bytes = (uint32_t)(Cfg::A_BYTES + (last ? tail : BN) * BK * 2);
                 bool ok = true;
                 for (int kb = 0; kb < nk; ++kb) {
                     if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, p.status, ERR_WAIT_SMEM_EMPTY)) { ok = false; break; }
-                    mbar_arrive_expect_tx(&full[s], Cfg::STAGE_BYTES);
+                    mbar_arrive_expect_tx(&full[s], bytes);
                     tma_load_2d(sA + s * Cfg::A_BYTES, &tmA, kb * BK, m0, &full[s]);
-                    tma_load_2d(sB + s * Cfg::B_BYTES, &tmB, kb * BK, n0, &full[s]);
+                    tma_load_2d(sB + s * Cfg::B_BYTES, tb, kb * BK, n0, &full[s]);
                     if (++s == S) { s = 0; ph ^= 1; }
                 }
                 if (!ok) break;
@@ -246,11 +260,13 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            constexpr uint32_t idesc = umma_idesc_bf16(BM, BN);
+            constexpr uint32_t idesc_full = umma_idesc_bf16(BM, BN);
+            const uint32_t idesc_tail = umma_idesc_bf16(BM, tail);
             int s = 0;
             uint32_t ph = 0;
             int tl = 0;
             for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++tl) {
+                const uint32_t idesc = t % num_n == num_n - 1 ? idesc_tail : idesc_full;
                 const int buf = tl & 1;
                 const uint32_t use = (uint32_t)(tl >> 1);
                 if (!mbar_wait(&tempty[buf], (use & 1) ^ 1, abort_flag, p.status, ERR_WAIT_TMEM_EMPTY)) break;
@@ -278,11 +294,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     } else {
         // epilogue warps 2..9: TMEM lane quadrant = warp % 4, column half = (warp - 2) / 4
         const int quad = warp & 3, e = warp - 2, half = e >> 2;
-        const int c0 = half ? epi_split<BN>() : 0, c1 = half ? BN : epi_split<BN>();
         uint8_t *stage = staging + e * (32 * 64);
         int tl = 0;
         for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++tl) {
-            const int m0 = (t / num_n) * BM, n0 = (t % num_n) * BN;
+            const int nt = t % num_n, m0 = (t / num_n) * BM, n0 = nt * BN;
+            const int w = nt == num_n - 1 ? tail : BN;
+            const int c0 = half ? epi_split(w) : 0, c1 = half ? w : epi_split(w);
             const int buf = tl & 1;
             const uint32_t use = (uint32_t)(tl >> 1);
             const uint32_t tbase = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * BN);
@@ -801,14 +818,20 @@ template <int BN> static void launch_bn(const GemmArgs &p, const bf16 *A, int ld
         if (e != cudaSuccess) throw std::runtime_error(std::string("gemm smem attribute: ") + cudaGetErrorString(e));
         attr_set[dev & 63] = true;
     }
-    CUtensorMap ta, tb;
+    const int num_n = (p.N + BN - 1) / BN;
+    const int tail = p.N - (num_n - 1) * BN;
+    if (tail % 16 || tail < 16) throw std::runtime_error("gemm: N must be a multiple of 16");
+    CUtensorMap ta, tb, tbt;
     make_tmap(&ta, A, (uint64_t)p.M, (uint64_t)p.K, (uint64_t)lda, BM);
-    make_tmap(&tb, W, (uint64_t)p.N, (uint64_t)p.K, (uint64_t)p.K, BN);
-    const int ntiles = ((p.M + BM - 1) / BM) * (p.N / BN);
+    // (one tile narrower than BN: both maps get the tail's box, never wider than N)
+    make_tmap(&tb, W, (uint64_t)p.N, (uint64_t)p.K, (uint64_t)p.K, num_n == 1 ? (uint32_t)tail : (uint32_t)BN);
+    if (tail != BN) make_tmap(&tbt, W, (uint64_t)p.N, (uint64_t)p.K, (uint64_t)p.K, (uint32_t)tail);
+    else tbt = tb;
+    const int ntiles = ((p.M + BM - 1) / BM) * num_n;
     int grid = std::min(ntiles, num_sms());
     if (max_ctas > 0) grid = std::min(grid, max_ctas);
     if (grid < 1) grid = 1;
-    k_gemm_bf16<BN><<<grid, GEMM_THREADS, Cfg::SMEM_BYTES, st>>>(ta, tb, p);
+    k_gemm_bf16<BN><<<grid, GEMM_THREADS, Cfg::SMEM_BYTES, st>>>(ta, tb, tbt, p);
 }
 
 template <int BN> static void launch_pair(const GemmArgs &p, const bf16 *A, int lda, const bf16 *W, cudaStream_t st,
@@ -868,6 +891,13 @@ int gemm_default_variant() {
 }
 
 int gemm_pick_bn(int N) {
+    if (N % 16 || N <= 0) return 0;
+    if (N == 128) return 128;  // the smaller B stage leaves room for 6 pipeline stages
+    return 256;                // 256-wide tiles, the last one narrower when 256 does not divide N
+}
+
+// The CTA-pair kernel needs BN | N (no tail tile).
+static int gemm_pick_bn_pair(int N) {
     if (N % 256 == 0) return 256;
     if (N % 240 == 0) return 240;
     if (N % 160 == 0) return 160;
@@ -879,15 +909,16 @@ void launch_gemm(const GemmArgs &p, const bf16 *A, int lda, const bf16 *W, cudaS
                  int variant) {
     if (p.M <= 0) return;
     if (p.K % BK) throw std::runtime_error("gemm: K must be a multiple of 64");
-    if (bn == 0) bn = gemm_pick_bn(p.N);
-    if (bn == 0 || p.N % bn) throw std::runtime_error("gemm: unsupported N " + std::to_string(p.N));
+    if (variant == 0) variant = gemm_default_variant();
+    if (bn == 0) bn = variant == 2 ? gemm_pick_bn_pair(p.N) : gemm_pick_bn(p.N);
+    if (bn == 0 || p.N % 16 || (variant == 2 && p.N % bn))
+        throw std::runtime_error("gemm: unsupported N " + std::to_string(p.N));
     if (p.ldo % 8 || (p.res && p.ldr % 8)) throw std::runtime_error("gemm: output/residual pitch must be 16-byte aligned");
     if (p.ln_g) {
         if (p.N != LN_N || !p.ln_b || p.pe_doy) throw std::runtime_error("gemm: LayerNorm epilogue needs N = 640");
         launch_ln(p, A, lda, W, st);
         return;
     }
-    if (variant == 0) variant = gemm_default_variant();
     if (variant == 2) {
         switch (bn) {
         case 256: launch_pair<256>(p, A, lda, W, st, max_ctas); return;
@@ -899,7 +930,6 @@ void launch_gemm(const GemmArgs &p, const bf16 *A, int lda, const bf16 *W, cudaS
     }
     switch (bn) {
     case 256: launch_bn<256>(p, A, lda, W, st, max_ctas); break;
-    case 240: launch_bn<240>(p, A, lda, W, st, max_ctas); break;
     case 160: launch_bn<160>(p, A, lda, W, st, max_ctas); break;
     case 128: launch_bn<128>(p, A, lda, W, st, max_ctas); break;
     default: throw std::runtime_error("gemm: unsupported tile width " + std::to_string(bn));

@@ -31,7 +31,8 @@ struct GemmArgs {
     const float *ln_b = nullptr;
 };
 
-// Tile width BN used for a given N (0 = unsupported).
+// Tile width BN used for a given N by the single-CTA kernel (0 = unsupported):
+// 256, with a narrower last tile when 256 does not divide N; 128 for N = 128.
 int gemm_pick_bn(int N);
 
 // Kernel used when launch_gemm is asked for variant 0: 1 = single CTA

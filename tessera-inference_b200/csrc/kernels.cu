@@ -374,40 +374,55 @@ __device__ __forceinline__ float half_sum(float v) {
 
 __global__ void __launch_bounds__(256) k_layernorm640(const bf16 *__restrict__ x, int64_t M, const float *__restrict__ g,
                                                       const float *__restrict__ b, bf16 *__restrict__ y) {
-    const int64_t r = (int64_t)blockIdx.x * 16 + (threadIdx.x >> 4);
-    const int sub = threadIdx.x & 15;
-    const bool live = r < M;
-    const bf16 *xr = x + (live ? r : 0) * D;
-    float v[40];
-#pragma unroll
-    for (int j = 0; j < 5; ++j) {
-        uint4 q = make_uint4(0, 0, 0, 0);
-        if (live) q = *reinterpret_cast<const uint4 *>(xr + j * 128 + sub * 8);
-        const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-        for (int k = 0; k < 4; ++k) { v[8 * j + 2 * k] = bf16lo(w[k]); v[8 * j + 2 * k + 1] = bf16hi(w[k]); }
+    // Grid-stride over row pairs: each warp takes two rows per trip (one per
+    // half-warp), so both halves run the same number of trips and the
+    // half-warp shuffles stay uniform. gamma/beta are read once per block into
+    // shared memory.
+    __shared__ __align__(16) float gs[D], bs[D];
+    for (int i = threadIdx.x; i < D; i += blockDim.x) {
+        gs[i] = g ? g[i] : 1.f;
+        bs[i] = g ? b[i] : 0.f;
     }
-    float s = 0.f;
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, sub = lane & 15, hw = lane >> 4;
+    const int64_t stride = (int64_t)gridDim.x * (blockDim.x >> 5) * 2;
+    for (int64_t base = ((int64_t)blockIdx.x * (blockDim.x >> 5) + warp) * 2; base < M; base += stride) {
+        const int64_t r = base + hw;
+        const bool live = r < M;
+        const bf16 *xr = x + (live ? r : 0) * D;
+        float v[40];
 #pragma unroll
-    for (int j = 0; j < 40; ++j) s += v[j];
-    const float mean = half_sum(s) / (float)D;
-    float q = 0.f;
+        for (int j = 0; j < 5; ++j) {
+            uint4 q = make_uint4(0, 0, 0, 0);
+            if (live) q = *reinterpret_cast<const uint4 *>(xr + j * 128 + sub * 8);
+            const uint32_t w[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-    for (int j = 0; j < 40; ++j) { const float d = v[j] - mean; q += d * d; }
-    const float rstd = 1.f / sqrtf(half_sum(q) / (float)D + LN_EPS);
-    if (!live) return;
-    bf16 *yr = y + r * D;
-#pragma unroll
-    for (int j = 0; j < 5; ++j) {
-        const int c = j * 128 + sub * 8;
-        float o[8];
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-            o[k] = (v[8 * j + k] - mean) * rstd;
-            if (g) o[k] = o[k] * __ldg(g + c + k) + __ldg(b + c + k);
+            for (int k = 0; k < 4; ++k) { v[8 * j + 2 * k] = bf16lo(w[k]); v[8 * j + 2 * k + 1] = bf16hi(w[k]); }
         }
-        *reinterpret_cast<uint4 *>(yr + c) = make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]),
-                                                        pack_bf16x2(o[4], o[5]), pack_bf16x2(o[6], o[7]));
+        float s = 0.f;
+#pragma unroll
+        for (int j = 0; j < 40; ++j) s += v[j];
+        const float mean = half_sum(s) / (float)D;
+        float q = 0.f;
+#pragma unroll
+        for (int j = 0; j < 40; ++j) { const float d = v[j] - mean; q += d * d; }
+        const float rstd = 1.f / sqrtf(half_sum(q) / (float)D + LN_EPS);
+        if (live) {
+            bf16 *yr = y + r * D;
+#pragma unroll
+            for (int j = 0; j < 5; ++j) {
+                const int c = j * 128 + sub * 8;
+                const float4 g0 = *reinterpret_cast<const float4 *>(gs + c), g1 = *reinterpret_cast<const float4 *>(gs + c + 4);
+                const float4 b0 = *reinterpret_cast<const float4 *>(bs + c), b1 = *reinterpret_cast<const float4 *>(bs + c + 4);
+                const float gg[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+                const float bb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+                float o[8];
+#pragma unroll
+                for (int k = 0; k < 8; ++k) o[k] = (v[8 * j + k] - mean) * rstd * gg[k] + bb[k];
+                *reinterpret_cast<uint4 *>(yr + c) = make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]),
+                                                                pack_bf16x2(o[4], o[5]), pack_bf16x2(o[6], o[7]));
+            }
+        }
     }
 }
 
@@ -849,7 +864,8 @@ void launch_attention(const bf16 *qkv, Segs segs, int64_t npix, int Tmax, bf16 *
 
 void launch_layernorm640(const bf16 *x, int64_t M, const float *g, const float *b, bf16 *y, cudaStream_t st) {
     if (M <= 0) return;
-    k_layernorm640<<<blocks_for(M, 16), 256, 0, st>>>(x, M, g, b, y);
+    const unsigned grid = (unsigned)std::min<int64_t>(blocks_for(M, 16), 148 * 8);
+    k_layernorm640<<<grid, 256, 0, st>>>(x, M, g, b, y);
     check_launch("k_layernorm640");
 }
 

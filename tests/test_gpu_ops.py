@@ -127,6 +127,28 @@ def test_gemm_tile_widths(lib, bn, variant):
     check_bf16(out, ref, mag)
 
 
+@pytest.mark.parametrize("N,bn", [(1200, 256), (400, 0), (48, 0), (640, 0), (1920, 0), (1200, 160), (208, 128)])
+def test_gemm_tail_tile(lib, N, bn):
+    """Column tiles of width bn with a narrower last tile (N not a multiple of
+    bn), through the residual epilogue: 1200 = 4*256 + 176, 400 = 256 + 144,
+    48 = one 48-wide tile, 640 = 256 + 256 + 128, 1200 = 7*160 + 80, 208 = 128 + 80."""
+    M, K = 1000, 640
+    g = torch.Generator(device="cuda").manual_seed(N + bn)
+    A = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
+    W = (torch.randn(N, K, device="cuda", generator=g) / K ** 0.5).to(torch.bfloat16)
+    bias = torch.randn(N, device="cuda", generator=g) * 0.1
+    res = torch.randn(M, N, device="cuda", generator=g).to(torch.bfloat16)
+    out = torch.full((M, N), float("nan"), device="cuda", dtype=torch.bfloat16)
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    rc = lib.tcb_op_gemm(_p(A), K, _p(W), _p(bias), 0, _p(res), N, None, 1, None, None, _p(out), N, M, N, K, bn, 1,
+                         _p(status), _stream())
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert status.item() == 0
+    ref, mag = gemm_ref(A, W, bias, False, res)
+    check_bf16(out, ref, mag)
+
+
 def test_gemm_pe_residual(lib):
     """Residual = bf16 day-of-year sinusoid: table rows for integer days in
     [0, 366], sin/cos of doy * div for any other value."""
