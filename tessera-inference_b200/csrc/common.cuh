@@ -102,6 +102,13 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *tm, in
         : "memory");
 }
 
+// Prefetch one box of a tensor map into L2 (no shared memory, nothing to wait for).
+__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap *tm, int c0, int c1) {
+    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(reinterpret_cast<uint64_t>(tm)),
+                 "r"(c0), "r"(c1)
+                 : "memory");
+}
+
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap *tm) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tm)) : "memory");
 }

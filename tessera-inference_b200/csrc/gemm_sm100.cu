@@ -41,6 +41,7 @@ constexpr int GEMM_THREADS = 320; // 10 warps: producer, MMA, 8 epilogue
 constexpr int EPI_WARPS = 8;      // two per TMEM lane quadrant, splitting the tile's columns
 constexpr int STAGING_BYTES = EPI_WARPS * 32 * 64;  // per epilogue warp: 32 rows x 32 bf16
 constexpr int SMEM_BUDGET = 225 * 1024;
+constexpr int RES_BOX = 128;      // residual L2-prefetch box: 128 columns x BM rows
 
 template <int BN> struct GemmCfg {
     static constexpr int A_BYTES = BM * BK * 2;
@@ -194,10 +195,13 @@ template <int BN> __host__ __device__ constexpr int epi_split() { return epi_spl
 // BN = 256 this keeps every MMA but the tail's at the full N = 256 issue width
 // (N = 640 -> 256, 256, 128), which runs faster than equal narrower tiles:
 // an M = 128, K = 16 MMA takes about as long at N = 128 or 160 as at N = 256.
+// With a residual matrix, the producer also prefetches each tile's residual
+// block into L2 (tmR, boxes of 128 x 128) when it starts loading the tile, so
+// the epilogue's residual reads, a tile later, hit L2 instead of HBM.
 template <int BN>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     k_gemm_bf16(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                const __grid_constant__ CUtensorMap tmBt, GemmArgs p) {
+                const __grid_constant__ CUtensorMap tmBt, const __grid_constant__ CUtensorMap tmR, GemmArgs p) {
     using Cfg = GemmCfg<BN>;
     constexpr int S = Cfg::STAGES;
     extern __shared__ uint8_t smem_raw[];
@@ -225,6 +229,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         prefetch_tensormap(&tmA);
         prefetch_tensormap(&tmB);
         if (tail != BN) prefetch_tensormap(&tmBt);
+        if (p.res) prefetch_tensormap(&tmR);
     }
     if (warp == 1) { tmem_alloc(tmem_holder, 512); tmem_relinquish(); }
     tc_fence_before();
@@ -241,6 +246,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                 const bool last = nt == num_n - 1;
                 const CUtensorMap *tb = last ? &tmBt : &tmB;
                 const uint32_t bytes = (uint32_t)(Cfg::A_BYTES + (last ? tail : BN) * BK * 2);
+                if (p.res)
+                    for (int x = 0; x < (last ? tail : BN); x += RES_BOX) tma_prefetch_l2_2d(&tmR, n0 + x, m0);
                 bool ok = true;
                 for (int kb = 0; kb < nk; ++kb) {
                     if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, p.status, ERR_WAIT_SMEM_EMPTY)) { ok = false; break; }
@@ -778,22 +785,28 @@ static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
     return fn;
 }
 
-// 2-D bf16 tensor map over a row-major [rows, cols] matrix (cols contiguous),
-// box = [box_rows, 64 columns], 128-byte swizzle. Rows past `rows` read as zero.
-static void make_tmap(CUtensorMap *tm, const void *ptr, uint64_t rows, uint64_t cols, uint64_t ld_elems,
-                      uint32_t box_rows) {
+// 2-D bf16 tensor map over a row-major [rows, cols] matrix (cols contiguous)
+// with the given box and swizzle. Rows past `rows` read as zero.
+static void make_tmap_box(CUtensorMap *tm, const void *ptr, uint64_t rows, uint64_t cols, uint64_t ld_elems,
+                          uint32_t box_cols, uint32_t box_rows, CUtensorMapSwizzle swizzle) {
     auto enc = get_encode_fn();
     if (!enc) throw std::runtime_error("cuTensorMapEncodeTiled unavailable");
     if (reinterpret_cast<uintptr_t>(ptr) % 16) throw std::runtime_error("TMA base address not 16-byte aligned");
     if ((ld_elems * 2) % 16) throw std::runtime_error("TMA row pitch not a multiple of 16 bytes");
     cuuint64_t dims[2] = {cols, rows};
     cuuint64_t strides[1] = {ld_elems * 2};
-    cuuint32_t box[2] = {(cuuint32_t)BK, box_rows};
+    cuuint32_t box[2] = {box_cols, box_rows};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(ptr), dims, strides, box, estr,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
+}
+
+// The operand maps: box = [box_rows, 64 columns] (one 128-byte swizzle atom of K).
+static void make_tmap(CUtensorMap *tm, const void *ptr, uint64_t rows, uint64_t cols, uint64_t ld_elems,
+                      uint32_t box_rows) {
+    make_tmap_box(tm, ptr, rows, cols, ld_elems, BK, box_rows, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 static int num_sms() {
@@ -821,8 +834,11 @@ template <int BN> static void launch_bn(const GemmArgs &p, const bf16 *A, int ld
     const int num_n = (p.N + BN - 1) / BN;
     const int tail = p.N - (num_n - 1) * BN;
     if (tail % 16 || tail < 16) throw std::runtime_error("gemm: N must be a multiple of 16");
-    CUtensorMap ta, tb, tbt;
+    CUtensorMap ta, tb, tbt, tr;
     make_tmap(&ta, A, (uint64_t)p.M, (uint64_t)p.K, (uint64_t)lda, BM);
+    if (p.res) make_tmap_box(&tr, p.res, (uint64_t)p.M, (uint64_t)p.N, (uint64_t)p.ldr, (uint32_t)std::min(RES_BOX, p.N),
+                             BM, CU_TENSOR_MAP_SWIZZLE_NONE);
+    else tr = ta;
     // (one tile narrower than BN: both maps get the tail's box, never wider than N)
     make_tmap(&tb, W, (uint64_t)p.N, (uint64_t)p.K, (uint64_t)p.K, num_n == 1 ? (uint32_t)tail : (uint32_t)BN);
     if (tail != BN) make_tmap(&tbt, W, (uint64_t)p.N, (uint64_t)p.K, (uint64_t)p.K, (uint32_t)tail);
@@ -831,7 +847,7 @@ template <int BN> static void launch_bn(const GemmArgs &p, const bf16 *A, int ld
     int grid = std::min(ntiles, num_sms());
     if (max_ctas > 0) grid = std::min(grid, max_ctas);
     if (grid < 1) grid = 1;
-    k_gemm_bf16<BN><<<grid, GEMM_THREADS, Cfg::SMEM_BYTES, st>>>(ta, tb, tbt, p);
+    k_gemm_bf16<BN><<<grid, GEMM_THREADS, Cfg::SMEM_BYTES, st>>>(ta, tb, tbt, tr, p);
 }
 
 template <int BN> static void launch_pair(const GemmArgs &p, const bf16 *A, int lda, const bf16 *W, cudaStream_t st,

@@ -364,65 +364,62 @@ __global__ void __launch_bounds__(256, NTMAX <= 16 ? 2 : 1)
 }
 
 // ------------------------------------------------------------------ LayerNorm
-// Half-warp per row of 640: lane holds 8 columns at sub*8 + 128*j (16-byte
-// accesses). Two-pass f32 statistics.
-__device__ __forceinline__ float half_sum(float v) {
-#pragma unroll
-    for (int o = 8; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    return v;
-}
+// Warp per row of 640, two-pass f32 statistics.
 
 __global__ void __launch_bounds__(256) k_layernorm640(const bf16 *__restrict__ x, int64_t M, const float *__restrict__ g,
                                                       const float *__restrict__ b, bf16 *__restrict__ y) {
-    // Grid-stride over row pairs: each warp takes two rows per trip (one per
-    // half-warp), so both halves run the same number of trips and the
-    // half-warp shuffles stay uniform. gamma/beta are read once per block into
-    // shared memory.
+    // Grid-stride over rows, one warp per row: lane l holds columns
+    // 128j + 4l .. 128j + 4l + 3 (j = 0..4) packed as bf16, so each 8-byte
+    // load instruction of the warp reads 256 contiguous bytes. The next row is
+    // loaded before the current one is reduced, which keeps two rows (2.5 KB)
+    // of loads in flight per warp at a low register count. gamma/beta are read
+    // once per block into shared memory.
     __shared__ __align__(16) float gs[D], bs[D];
     for (int i = threadIdx.x; i < D; i += blockDim.x) {
         gs[i] = g ? g[i] : 1.f;
         bs[i] = g ? b[i] : 0.f;
     }
     __syncthreads();
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, sub = lane & 15, hw = lane >> 4;
-    const int64_t stride = (int64_t)gridDim.x * (blockDim.x >> 5) * 2;
-    for (int64_t base = ((int64_t)blockIdx.x * (blockDim.x >> 5) + warp) * 2; base < M; base += stride) {
-        const int64_t r = base + hw;
-        const bool live = r < M;
-        const bf16 *xr = x + (live ? r : 0) * D;
-        float v[40];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t stride = (int64_t)gridDim.x * (blockDim.x >> 5);
+    auto load = [&](int64_t r, uint2 (&q)[5]) {
+        const bf16 *xr = x + r * D + lane * 4;
 #pragma unroll
-        for (int j = 0; j < 5; ++j) {
-            uint4 q = make_uint4(0, 0, 0, 0);
-            if (live) q = *reinterpret_cast<const uint4 *>(xr + j * 128 + sub * 8);
-            const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-            for (int k = 0; k < 4; ++k) { v[8 * j + 2 * k] = bf16lo(w[k]); v[8 * j + 2 * k + 1] = bf16hi(w[k]); }
-        }
+        for (int j = 0; j < 5; ++j) q[j] = *reinterpret_cast<const uint2 *>(xr + j * 128);
+    };
+    int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp;
+    uint2 q[5], qn[5];
+    if (r < M) load(r, q);
+    for (; r < M; r += stride) {
+        if (r + stride < M) load(r + stride, qn);
         float s = 0.f;
 #pragma unroll
-        for (int j = 0; j < 40; ++j) s += v[j];
-        const float mean = half_sum(s) / (float)D;
-        float q = 0.f;
-#pragma unroll
-        for (int j = 0; j < 40; ++j) { const float d = v[j] - mean; q += d * d; }
-        const float rstd = 1.f / sqrtf(half_sum(q) / (float)D + LN_EPS);
-        if (live) {
-            bf16 *yr = y + r * D;
-#pragma unroll
-            for (int j = 0; j < 5; ++j) {
-                const int c = j * 128 + sub * 8;
-                const float4 g0 = *reinterpret_cast<const float4 *>(gs + c), g1 = *reinterpret_cast<const float4 *>(gs + c + 4);
-                const float4 b0 = *reinterpret_cast<const float4 *>(bs + c), b1 = *reinterpret_cast<const float4 *>(bs + c + 4);
-                const float gg[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
-                const float bb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
-                float o[8];
-#pragma unroll
-                for (int k = 0; k < 8; ++k) o[k] = (v[8 * j + k] - mean) * rstd * gg[k] + bb[k];
-                *reinterpret_cast<uint4 *>(yr + c) = make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]),
-                                                                pack_bf16x2(o[4], o[5]), pack_bf16x2(o[6], o[7]));
-            }
+        for (int j = 0; j < 5; ++j) {
+            s += bf16lo(q[j].x); s += bf16hi(q[j].x);
+            s += bf16lo(q[j].y); s += bf16hi(q[j].y);
         }
+        const float mean = warp_sum(s) / (float)D;
+        float ss = 0.f;
+#pragma unroll
+        for (int j = 0; j < 5; ++j) {
+            const float d0 = bf16lo(q[j].x) - mean, d1 = bf16hi(q[j].x) - mean;
+            const float d2 = bf16lo(q[j].y) - mean, d3 = bf16hi(q[j].y) - mean;
+            ss += d0 * d0; ss += d1 * d1; ss += d2 * d2; ss += d3 * d3;
+        }
+        const float rstd = 1.f / sqrtf(warp_sum(ss) / (float)D + LN_EPS);
+        bf16 *yr = y + r * D + lane * 4;
+#pragma unroll
+        for (int j = 0; j < 5; ++j) {
+            const int c = j * 128 + lane * 4;
+            const float4 gg = *reinterpret_cast<const float4 *>(gs + c), bb = *reinterpret_cast<const float4 *>(bs + c);
+            const uint32_t o0 = pack_bf16x2((bf16lo(q[j].x) - mean) * rstd * gg.x + bb.x,
+                                            (bf16hi(q[j].x) - mean) * rstd * gg.y + bb.y);
+            const uint32_t o1 = pack_bf16x2((bf16lo(q[j].y) - mean) * rstd * gg.z + bb.z,
+                                            (bf16hi(q[j].y) - mean) * rstd * gg.w + bb.w);
+            *reinterpret_cast<uint2 *>(yr + j * 128) = make_uint2(o0, o1);
+        }
+#pragma unroll
+        for (int j = 0; j < 5; ++j) q[j] = qn[j];
     }
 }
 
@@ -864,7 +861,17 @@ void launch_attention(const bf16 *qkv, Segs segs, int64_t npix, int Tmax, bf16 *
 
 void launch_layernorm640(const bf16 *x, int64_t M, const float *g, const float *b, bf16 *y, cudaStream_t st) {
     if (M <= 0) return;
-    const unsigned grid = (unsigned)std::min<int64_t>(blocks_for(M, 16), 148 * 8);
+    // grid-stride: as many blocks as fit on the device at once
+    static int resident[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!resident[dev & 63]) {
+        int per_sm = 0, sms = 0;
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_layernorm640, 256, 0);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        resident[dev & 63] = std::max(1, per_sm) * std::max(1, sms);
+    }
+    const unsigned grid = (unsigned)std::min<int64_t>(blocks_for(M, 8), resident[dev & 63]);
     k_layernorm640<<<grid, 256, 0, st>>>(x, M, g, b, y);
     check_launch("k_layernorm640");
 }
