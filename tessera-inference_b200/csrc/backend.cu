@@ -383,7 +383,7 @@ static void backbone(Dev &d, int b, const float *rec, Segs segs, int64_t M, int 
         for (int l = 0; l < NL; ++l) {
             gemm(d, GK_QKV, B.qkv[l], d.x.p, M, d.qkv.p, false);
             d.mark(TC_CAT_ATTN);
-            launch_attention(d.qkv.p, segs, npix, Tmax, d.att.p, d.st);
+            launch_attention(d.qkv.p, segs, npix, M, Tmax, d.att.p, d.status.p, d.st);
             if (ln_fused()) {  // LN1 / LN2 in the epilogues of out-proj / FFN2
                 gemm(d, GK_OUT, B.out[l], d.att.p, M, d.x1.p, false, d.x.p, nullptr, 1, B.ln1g[l], B.ln1b[l]);
                 gemm(d, GK_FFN1, B.ffn1[l], d.x1.p, M, d.hbuf.p, true);
@@ -959,8 +959,13 @@ int tcb_op_emb1(int C, const float *rec, int64_t M, const float *w1t, const floa
 
 int tcb_op_attention(const void *qkv, const int64_t *off, int64_t uniform_T, int64_t npix, int Tmax, void *att,
                      void *stream) {
-    OP_TRY("tcb_op_attention", launch_attention(static_cast<const bf16 *>(qkv), Segs{off, 0, uniform_T}, npix, Tmax,
-                                                static_cast<bf16 *>(att), static_cast<cudaStream_t>(stream)))
+    OP_TRY("tcb_op_attention", {
+        // the qkv rows the segments reach: off[npix] (read back), or npix * uniform_T
+        int64_t ntok = npix * uniform_T;
+        if (off && npix > 0) CK(cudaMemcpy(&ntok, off + npix, sizeof(int64_t), cudaMemcpyDeviceToHost));
+        launch_attention(static_cast<const bf16 *>(qkv), Segs{off, 0, uniform_T}, npix, ntok, Tmax,
+                         static_cast<bf16 *>(att), nullptr, static_cast<cudaStream_t>(stream));
+    })
 }
 
 int tcb_op_layernorm640(const void *x, int64_t M, const float *g, const float *b, void *y, void *stream) {

@@ -787,8 +787,8 @@ static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
 
 // 2-D bf16 tensor map over a row-major [rows, cols] matrix (cols contiguous)
 // with the given box and swizzle. Rows past `rows` read as zero.
-static void make_tmap_box(CUtensorMap *tm, const void *ptr, uint64_t rows, uint64_t cols, uint64_t ld_elems,
-                          uint32_t box_cols, uint32_t box_rows, CUtensorMapSwizzle swizzle) {
+void make_tmap_box(CUtensorMap *tm, const void *ptr, uint64_t rows, uint64_t cols, uint64_t ld_elems,
+                   uint32_t box_cols, uint32_t box_rows, CUtensorMapSwizzle swizzle) {
     auto enc = get_encode_fn();
     if (!enc) throw std::runtime_error("cuTensorMapEncodeTiled unavailable");
     if (reinterpret_cast<uintptr_t>(ptr) % 16) throw std::runtime_error("TMA base address not 16-byte aligned");

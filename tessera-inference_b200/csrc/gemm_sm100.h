@@ -1,6 +1,7 @@
 // Host interface of the tcgen05 GEMM (gemm_sm100.cu).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -30,6 +31,11 @@ struct GemmArgs {
     const float *ln_g = nullptr;
     const float *ln_b = nullptr;
 };
+
+// 2-D bf16 tensor map over a row-major [rows, cols] matrix with row pitch
+// ld_elems, the given box and swizzle. Throws on misaligned base or pitch.
+void make_tmap_box(CUtensorMap *tm, const void *ptr, uint64_t rows, uint64_t cols, uint64_t ld_elems,
+                   uint32_t box_cols, uint32_t box_rows, CUtensorMapSwizzle swizzle);
 
 // Tile width BN used for a given N by the single-CTA kernel (0 = unsupported):
 // 256, with a narrower last tile when 256 does not divide N; 128 for N = 128.

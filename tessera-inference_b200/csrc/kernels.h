@@ -46,8 +46,11 @@ void launch_emb1(int C, const float *rec, int64_t M, const float *w1t, const flo
                  cudaStream_t st);
 
 // Self-attention of every pixel segment, 4 heads x 160, no mask (tessera_cpu.cpp:410-418).
-void launch_attention(const __nv_bfloat16 *qkv, Segs segs, int64_t npix, int Tmax, __nv_bfloat16 *att,
-                      cudaStream_t st);
+// qkv holds ntok token rows of 1920 (the rows the segments index). Series of
+// up to 128 steps run on the tcgen05 kernel, whose bounded waits report into
+// *status (may be null); longer ones on the mma.sync kernel.
+void launch_attention(const __nv_bfloat16 *qkv, Segs segs, int64_t npix, int64_t ntok, int Tmax, __nv_bfloat16 *att,
+                      int *status, cudaStream_t st);
 
 // y = bf16(LN(x) * g + b) over rows of 640 (g, b may be null for no affine).
 void launch_layernorm640(const __nv_bfloat16 *x, int64_t M, const float *g, const float *b, __nv_bfloat16 *y,

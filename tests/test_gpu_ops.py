@@ -198,11 +198,30 @@ def attention_ref(qkv, off):
                                   [120] * 300 + [0, 3, 128, 1],
                                   [8, 16, 24, 40, 56, 72, 88, 96] * 40])
 def test_attention_segments(lib, lens):
-    """Default per-(pixel, head) kernel; the pipelined kernel is checked in
-    tests/test_gpu_variants.py (it is selected by environment at load time)."""
+    """Series of up to 128 steps run on the tcgen05 kernel (the 2nd and 3rd
+    cases), longer ones on the mma.sync kernel (the 1st); the other kernels are
+    checked in tests/test_gpu_variants.py (selected by environment at load)."""
     off = np.concatenate([[0], np.cumsum(lens)]).astype(np.int64)
     M = int(off[-1])
     g = torch.Generator(device="cuda").manual_seed(11)
+    qkv = torch.randn(M, 1920, device="cuda", generator=g).to(torch.bfloat16)
+    att = torch.zeros(M, 640, device="cuda", dtype=torch.bfloat16)
+    doff = torch.from_numpy(off).cuda()
+    rc = lib.tcb_op_attention(_p(qkv), _p(doff), 0, len(lens), max(lens), _p(att), _stream())
+    assert rc == 0
+    torch.cuda.synchronize()
+    close_bf16(att, attention_ref(qkv, off), ulps=3, atol=1e-2)
+
+
+def test_attention_tc_stage_reuse(lib):
+    """tcgen05 kernel: many more items than CTAs, so both K/V stages and both
+    S/P buffers are reused, with empty pixels and every length class of 16
+    interleaved, and a 32-row box boundary at T = 32, 64, 96."""
+    rng = np.random.default_rng(3)
+    lens = list(rng.integers(0, 129, size=2000)) + [32, 64, 96, 128, 31, 33, 1, 0]
+    off = np.concatenate([[0], np.cumsum(lens)]).astype(np.int64)
+    M = int(off[-1])
+    g = torch.Generator(device="cuda").manual_seed(21)
     qkv = torch.randn(M, 1920, device="cuda", generator=g).to(torch.bfloat16)
     att = torch.zeros(M, 640, device="cuda", dtype=torch.bfloat16)
     doff = torch.from_numpy(off).cuda()
