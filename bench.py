@@ -51,6 +51,11 @@ import synth  # noqa: E402
 METRIC = "pixels/sec (tiles/hour) per B200 and whole box at 1/2/4/8 GPUs vs ref CPU"
 UNIT = "px/s"
 WORKLOAD = "config 1: synthetic Manchester-sized tile 1113x695 (773,535 px), T2=120 (60% valid), Ta=Td=60"
+# DRAM bytes per GEMM FLOP over all k_gemm_bf16 launches of one ncu capture
+# (dram__bytes_read.sum + dram__bytes_write.sum; profiles/k_gemm_bf16_ffn1_config0.md),
+# and the algorithmic bytes per FLOP of the layer mix (QKV, out-proj, FFN1, FFN2).
+GEMM_DRAM_BYTES_PER_FLOP = 2.15e-3
+GEMM_ALG_BYTES_PER_FLOP = 2.34e-3
 SMI_FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -405,7 +410,13 @@ def main():
                      "frac": gemm_tflops / peak if gemm_tflops else None,
                      "peak_source": f"{peaks['source']} bf16 sustained (kernel timed inside a long step)",
                      "measured": "per-launch CUDA events on the library stream over one profiled step after the timed steps",
-                     "traffic": None,
+                     "traffic": (GEMM_DRAM_BYTES_PER_FLOP * st["gemm_flop"] / st["gemm_launches"]
+                                 if st.get("gemm_launches") else None),
+                     "traffic_unit": "DRAM bytes per GEMM launch",
+                     "traffic_source": "ncu capture of every GEMM launch of config 0 (DRAM bytes per FLOP), "
+                                       "scaled by this run's FLOP per launch",
+                     "algorithmic_bytes_per_launch": (GEMM_ALG_BYTES_PER_FLOP * st["gemm_flop"] / st["gemm_launches"]
+                                                      if st.get("gemm_launches") else None),
                      "end_to_end_tflops": alg_tflops, "end_to_end_frac": alg_tflops / peak},
         "phase_ms_per_step": cat, "profiled_step_ms": prof_ms,
         "gemm_tflops_by_layer": {k: (v["flop"] / (v["ms"] * 1e-3) / 1e12 if v["ms"] > 0 else None)

@@ -580,15 +580,18 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
                 store_q();  // S(j) has consumed Q(j)
                 if (it3 < nitems) load_q(t0nn, Tnn, hnn);
             }
+            // 16-column halves past Tpad are skipped (the branch is uniform per warp)
             float mx = -INFINITY;
 #pragma unroll
             for (int q = 0; q < 2; ++q)
+                if (c0 + q * 16 < tpad) {
 #pragma unroll
-                for (int k = 0; k < 16; ++k) {
-                    const int col = c0 + q * 16 + k;
-                    const float x = col < T ? bf16_round(__uint_as_float(v[q][k]) * scale) : -INFINITY;
-                    v[q][k] = __float_as_uint(x);
-                    mx = fmaxf(mx, x);
+                    for (int k = 0; k < 16; ++k) {
+                        const int col = c0 + q * 16 + k;
+                        const float x = col < T ? bf16_round(__uint_as_float(v[q][k]) * scale) : -INFINITY;
+                        v[q][k] = __float_as_uint(x);
+                        mx = fmaxf(mx, x);
+                    }
                 }
             red_max[slice * 128 + r] = mx;
             named_bar_sync(1 + quad, 128);
@@ -596,11 +599,13 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
             float z = 0.f;
 #pragma unroll
             for (int q = 0; q < 2; ++q)
+                if (c0 + q * 16 < tpad) {
 #pragma unroll
-                for (int k = 0; k < 16; ++k) {
-                    const float ex = expf(__uint_as_float(v[q][k]) - mx);  // 0 for masked columns
-                    v[q][k] = __float_as_uint(ex);
-                    z += ex;
+                    for (int k = 0; k < 16; ++k) {
+                        const float ex = expf(__uint_as_float(v[q][k]) - mx);  // 0 for masked columns
+                        v[q][k] = __float_as_uint(ex);
+                        z += ex;
+                    }
                 }
             red_sum[slice * 128 + r] = z;
             named_bar_sync(1 + quad, 128);
@@ -1173,14 +1178,32 @@ static bool attention_pipelined() {
     return on;
 }
 
-// TC_ATTN_TC=0 keeps series of up to 128 steps on the mma.sync kernel too.
-static bool attention_tcgen05() {
-    static const bool on = [] {
+// TC_ATTN_TC: 0 = always the mma.sync kernel, 1 (default) = the cheaper of the
+// two by the cost model below, 2 = the tcgen05 kernel whenever T <= 128.
+static int attention_tcgen05() {
+    static const int mode = [] {
         const char *e = std::getenv("TC_ATTN_TC");
-        return !(e && *e == '0');
+        return e && (*e == '0' || *e == '2') ? *e - '0' : 1;
     }();
-    return on;
+    return mode;
 }
+
+// Kernel choice by cost per pixel (ns, all 4 heads), fitted to B200 timings
+// of 131,072-token chunks of uniform series length T:
+// * the mma.sync kernel sizes every CTA by the chunk's longest series, so its
+//   cost follows Tpad_max: 19, 38, 62, 89, 126, 179, 228, 266 ns at
+//   Tpad = 16, 32, ..., 128;
+// * the tcgen05 kernel pays a fixed cost per (pixel, head) item plus a little
+//   per key: about 35 + 1.3 * T_mean ns.
+// Uniform T = 80 stays on mma.sync (206 against 216 us per chunk), T = 96
+// moves to tcgen05 (205 against 244 us); a config-1 S2 chunk (T_mean ~ 72,
+// T_max ~ 104) goes to tcgen05 (225 against 260 us).
+static double attention_mma_cost_ns(int tpad) {
+    static const double c[8] = {19, 38, 62, 89, 126, 179, 228, 266};
+    const int i = std::min(std::max(tpad / 16, 1), 8) - 1;
+    return c[i];
+}
+static double attention_tc_cost_ns(double t_mean) { return 35.0 + 1.3 * t_mean; }
 
 static void attention_tc(const bf16 *qkv, Segs segs, int64_t npix, int64_t ntok, bf16 *att, int *status,
                          cudaStream_t st) {
@@ -1207,7 +1230,9 @@ void launch_attention(const bf16 *qkv, Segs segs, int64_t npix, int64_t ntok, in
     if (npix <= 0 || Tmax <= 0) return;
     if (Tmax > 256) throw std::runtime_error("attention: T > 256");
     const int Tpad = (Tmax + 15) & ~15;
-    if (Tpad <= 128 && ntok > 0 && attention_tcgen05() && !attention_pipelined()) {
+    const int tc_mode = attention_tcgen05();
+    const bool tc_cheaper = ntok > 0 && attention_tc_cost_ns(double(ntok) / double(npix)) < attention_mma_cost_ns(Tpad);
+    if (Tpad <= 128 && ntok > 0 && (tc_mode == 2 || (tc_mode == 1 && tc_cheaper)) && !attention_pipelined()) {
         attention_tc(qkv, segs, npix, ntok, att, status, st);
     } else if (attention_pipelined()) {
         if (Tpad <= 32) attention_pipe<4>(qkv, segs, npix, att, st);

@@ -198,9 +198,10 @@ def attention_ref(qkv, off):
                                   [120] * 300 + [0, 3, 128, 1],
                                   [8, 16, 24, 40, 56, 72, 88, 96] * 40])
 def test_attention_segments(lib, lens):
-    """Series of up to 128 steps run on the tcgen05 kernel (the 2nd and 3rd
-    cases), longer ones on the mma.sync kernel (the 1st); the other kernels are
-    checked in tests/test_gpu_variants.py (selected by environment at load)."""
+    """The 2nd and 3rd cases (series of at most 128 steps, long enough on
+    average) run on the tcgen05 kernel, the 1st (series up to 256) on the
+    mma.sync kernel. The forced selections are checked in
+    tests/test_gpu_variants.py (selected by environment at load)."""
     off = np.concatenate([[0], np.cumsum(lens)]).astype(np.int64)
     M = int(off[-1])
     g = torch.Generator(device="cuda").manual_seed(11)
@@ -218,7 +219,9 @@ def test_attention_tc_stage_reuse(lib):
     S/P buffers are reused, with empty pixels and every length class of 16
     interleaved, and a 32-row box boundary at T = 32, 64, 96."""
     rng = np.random.default_rng(3)
-    lens = list(rng.integers(0, 129, size=2000)) + [32, 64, 96, 128, 31, 33, 1, 0]
+    lens = (list(rng.integers(64, 129, size=1900)) + list(rng.integers(0, 64, size=100))
+            + [32, 64, 96, 128, 31, 33, 1, 0])
+    rng.shuffle(lens)
     off = np.concatenate([[0], np.cumsum(lens)]).astype(np.int64)
     M = int(off[-1])
     g = torch.Generator(device="cuda").manual_seed(21)
