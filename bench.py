@@ -51,9 +51,11 @@ import synth  # noqa: E402
 METRIC = "pixels/sec (tiles/hour) per B200 and whole box at 1/2/4/8 GPUs vs ref CPU"
 UNIT = "px/s"
 WORKLOAD = "config 1: synthetic Manchester-sized tile 1113x695 (773,535 px), T2=120 (60% valid), Ta=Td=60"
-# DRAM bytes per GEMM FLOP over all k_gemm_bf16 launches of one ncu capture
-# (dram__bytes_read.sum + dram__bytes_write.sum; profiles/k_gemm_bf16_ffn1_config0.md),
-# and the algorithmic bytes per FLOP of the layer mix (QKV, out-proj, FFN1, FFN2).
+# DRAM bytes per GEMM FLOP (dram__bytes_read.sum + dram__bytes_write.sum summed
+# over all 360 k_gemm_bf16 launches of one ncu capture of five config-0 encodes:
+# 126.5 GB for 58.9 TFLOP), and the algorithmic bytes per FLOP of the layer mix
+# (per token and layer QKV 5120 B, out-proj 3840 B, FFN1 6400 B, FFN2 7680 B over
+# 9.83 MFLOP).
 GEMM_DRAM_BYTES_PER_FLOP = 2.15e-3
 GEMM_ALG_BYTES_PER_FLOP = 2.34e-3
 SMI_FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
