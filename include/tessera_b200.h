@@ -86,6 +86,14 @@ int tc_encode_tile_device(void *h, const uint16_t *bands, const uint8_t *masks, 
 int tc_plan_rows(const uint8_t *masks, const int16_t *asc, const int16_t *desc, int64_t T2, int64_t Ta, int64_t Td,
                  int64_t H, int64_t W, int nparts, int64_t *row_bounds);
 
+/* Page-locked host memory usable by every device (cudaHostAllocPortable), so
+ * a caller's tile and output buffers are copied at full PCIe/C2C speed by the
+ * tile entry points without the caller linking the CUDA runtime itself.
+ * No reference counterpart. Returns NULL (and prints "tc_host_alloc: ...")
+ * on failure; tc_host_free(NULL) is a no-op. */
+void *tc_host_alloc(int64_t bytes);
+void tc_host_free(void *p);
+
 /* Run the handle's work on a caller-owned cudaStream_t (single-device
  * handles only); NULL restores the handle's own stream. Returns 0 or -1. */
 int tc_set_stream(void *h, void *stream);

@@ -816,6 +816,21 @@ int tc_plan_rows(const uint8_t *masks, const int16_t *asc, const int16_t *desc, 
     }
 }
 
+void *tc_host_alloc(int64_t bytes) {
+    if (bytes <= 0) return nullptr;
+    void *p = nullptr;
+    cudaError_t e = cudaHostAlloc(&p, (size_t)bytes, cudaHostAllocPortable);
+    if (e != cudaSuccess) {
+        std::fprintf(stderr, "tc_host_alloc: %s\n", cudaGetErrorString(e));
+        return nullptr;
+    }
+    return p;
+}
+
+void tc_host_free(void *p) {
+    if (p) cudaFreeHost(p);
+}
+
 int tc_set_stream(void *handle, void *stream) {
     if (!handle) return -1;
     Handle &h = *static_cast<Handle *>(handle);

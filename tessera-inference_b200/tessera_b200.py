@@ -20,7 +20,8 @@ LIB_PATH = PKG_DIR / "libtessera_b200.so"
 EXPORTED = [
     "tc_create", "tc_encode", "tc_profile_dump", "tc_destroy",
     "tc_create_multi", "tc_encode_tile", "tc_encode_tile_rows", "tc_encode_tile_device",
-    "tc_plan_rows", "tc_set_stream", "tc_set_profiling", "tc_get_stats", "tc_reset_stats",
+    "tc_plan_rows", "tc_set_stream", "tc_set_profiling", "tc_get_stats", "tc_reset_stats", "tc_host_alloc",
+    "tc_host_free",
     "tcb_op_gemm", "tcb_op_gemm_ln", "tcb_op_gemm_ln_noalloc", "tcb_op_count", "tcb_op_gather", "tcb_op_emb1", "tcb_op_attention",
     "tcb_op_layernorm640", "tcb_op_pool", "tcb_op_ln_relu2560", "tcb_op_out128", "tcb_op_wait_probe",
 ]
@@ -80,6 +81,10 @@ def load_library(path: os.PathLike | None = None) -> C.CDLL:
     lib.tc_plan_rows.argtypes = [vp, vp, vp, i64, i64, i64, i64, i64, i32, vp]
     lib.tc_set_stream.restype = i32
     lib.tc_set_stream.argtypes = [vp, vp]
+    lib.tc_host_alloc.restype = vp
+    lib.tc_host_alloc.argtypes = [i64]
+    lib.tc_host_free.restype = None
+    lib.tc_host_free.argtypes = [vp]
     lib.tc_set_profiling.restype = i32
     lib.tc_set_profiling.argtypes = [vp, i32]
     lib.tc_get_stats.restype = i32

@@ -118,3 +118,27 @@ def test_plan_rows_more_parts_than_rows():
     b = tb.plan_rows(tile, 8)
     assert b[0] == 0 and b[-1] == 3 and len(b) == 9
     assert all(x <= y for x, y in zip(b, b[1:]))
+
+
+DRIVER = REPO / "tessera-inference_b200" / "tessera_b200_encode"
+
+
+def test_tile_driver_cli_without_gpu(tmp_path):
+    """The tile driver (reference command line) prints its usage on missing
+    arguments and fails cleanly, naming the problem, on a bad weights file."""
+    import subprocess
+    assert DRIVER.exists(), "make -C tessera-inference_b200 builds tessera_b200_encode"
+    r = subprocess.run([str(DRIVER)], capture_output=True, text=True)
+    assert r.returncode == 2 and "usage:" in r.stderr
+    bad = tmp_path / "bad.tcw"
+    bad.write_bytes(b"NOPE")
+    r = subprocess.run([str(DRIVER), str(tmp_path / "tile"), str(tmp_path / "out"), str(bad)], capture_output=True,
+                       text=True)
+    assert r.returncode == 1 and "tc_create: bad weights file" in r.stderr
+
+
+def test_host_alloc_rejects_nonpositive():
+    lib = tb.load_library()
+    assert lib.tc_host_alloc(0) is None
+    assert lib.tc_host_alloc(-5) is None
+    lib.tc_host_free(None)
