@@ -146,34 +146,47 @@ __global__ void __launch_bounds__(128) k_gather(TileDev t, int64_t p0, int64_t n
 }
 
 // ------------------------------------------------------------------ emb1
-// Warp per token; lane computes columns lane*4 + 128*j (j < 5).
+// Warp per token pair; lane computes columns lane*4 + 128*j (j < 5) of two
+// tokens, so each float4 of weights read from shared memory serves both.
+// Every output is fmaf over k = 0..C-1 in order, then + bias, then ReLU.
 template <int C>
 __global__ void __launch_bounds__(256) k_emb1(const float *__restrict__ rec, int64_t M, const float *__restrict__ w1t,
                                               const float *__restrict__ b1, bf16 *__restrict__ y) {
-    __shared__ float ws[C * D];
-    __shared__ float bs[D];
+    __shared__ __align__(16) float ws[C * D];
+    __shared__ __align__(16) float bs[D];
     for (int i = threadIdx.x; i < C * D; i += blockDim.x) ws[i] = w1t[i];
     for (int i = threadIdx.x; i < D; i += blockDim.x) bs[i] = b1[i];
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
-    for (int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp; r < M; r += nwarps) {
-        float a[C];
+    for (int64_t r = ((int64_t)blockIdx.x * (blockDim.x >> 5) + warp) * 2; r < M; r += nwarps * 2) {
+        const bool two = r + 1 < M;
+        float a[2][C];
 #pragma unroll
-        for (int k = 0; k < C; ++k) a[k] = bf16_round(__ldg(rec + r * (C + 1) + k));
-        bf16 *yr = y + r * D;
+        for (int k = 0; k < C; ++k) {
+            a[0][k] = bf16_round(__ldg(rec + r * (C + 1) + k));
+            a[1][k] = two ? bf16_round(__ldg(rec + (r + 1) * (C + 1) + k)) : 0.f;
+        }
 #pragma unroll
         for (int j = 0; j < 5; ++j) {
             const int n = j * 128 + lane * 4;
-            float acc[4];
+            float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                float s = 0.f;
-#pragma unroll
-                for (int k = 0; k < C; ++k) s = fmaf(a[k], ws[k * D + n + q], s);
-                acc[q] = fmaxf(s + bs[n + q], 0.f);
+            for (int k = 0; k < C; ++k) {
+                const float4 wk = *reinterpret_cast<const float4 *>(ws + k * D + n);
+                s0[0] = fmaf(a[0][k], wk.x, s0[0]); s0[1] = fmaf(a[0][k], wk.y, s0[1]);
+                s0[2] = fmaf(a[0][k], wk.z, s0[2]); s0[3] = fmaf(a[0][k], wk.w, s0[3]);
+                s1[0] = fmaf(a[1][k], wk.x, s1[0]); s1[1] = fmaf(a[1][k], wk.y, s1[1]);
+                s1[2] = fmaf(a[1][k], wk.z, s1[2]); s1[3] = fmaf(a[1][k], wk.w, s1[3]);
             }
-            *reinterpret_cast<uint2 *>(yr + n) = make_uint2(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]));
+            const float4 bb = *reinterpret_cast<const float4 *>(bs + n);
+            *reinterpret_cast<uint2 *>(y + r * D + n) =
+                make_uint2(pack_bf16x2(fmaxf(s0[0] + bb.x, 0.f), fmaxf(s0[1] + bb.y, 0.f)),
+                           pack_bf16x2(fmaxf(s0[2] + bb.z, 0.f), fmaxf(s0[3] + bb.w, 0.f)));
+            if (two)
+                *reinterpret_cast<uint2 *>(y + (r + 1) * D + n) =
+                    make_uint2(pack_bf16x2(fmaxf(s1[0] + bb.x, 0.f), fmaxf(s1[1] + bb.y, 0.f)),
+                               pack_bf16x2(fmaxf(s1[2] + bb.z, 0.f), fmaxf(s1[3] + bb.w, 0.f)));
         }
     }
 }
@@ -771,7 +784,6 @@ __global__ void __launch_bounds__(256) k_layernorm640(const bf16 *__restrict__ x
 __global__ void __launch_bounds__(160) k_pool(const bf16 *__restrict__ x, Segs segs, const float *__restrict__ q,
                                               float qb, bf16 *__restrict__ fused, int col0) {
     __shared__ float w[256];
-    __shared__ float zs;
     const int64_t i = blockIdx.x;
     const int64_t t0 = seg_at(segs, i);
     const int T = (int)(seg_at(segs, i + 1) - t0);
@@ -801,17 +813,25 @@ __global__ void __launch_bounds__(160) k_pool(const bf16 *__restrict__ x, Segs s
         float z = 0.f;
         for (int t = lane; t < T; t += 32) { const float e = expf(w[t] - mx); w[t] = e; z += e; }
         z = warp_sum(z);
-        if (lane == 0) zs = z;
+        __syncwarp();
+        for (int t = lane; t < T; t += 32) w[t] = w[t] / z;  // the weights, each divided once
     }
     __syncthreads();
-    const float z = zs;
+    // p = sum_t w_t x_t in t order; four steps' loads are issued ahead of their FMAs
     const int c = threadIdx.x * 4;
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int t = 0; t < T; ++t) {
-        const float wt = w[t] / z;
-        const uint2 v = *reinterpret_cast<const uint2 *>(xp + (int64_t)t * D + c);
+    auto add = [&](float wt, uint2 v) {
         acc[0] += wt * bf16lo(v.x); acc[1] += wt * bf16hi(v.x); acc[2] += wt * bf16lo(v.y); acc[3] += wt * bf16hi(v.y);
+    };
+    int t = 0;
+    for (; t + 4 <= T; t += 4) {
+        uint2 v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) v[u] = *reinterpret_cast<const uint2 *>(xp + (int64_t)(t + u) * D + c);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) add(w[t + u], v[u]);
     }
+    for (; t < T; ++t) add(w[t], *reinterpret_cast<const uint2 *>(xp + (int64_t)t * D + c));
     *reinterpret_cast<uint2 *>(fo + c) = make_uint2(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]));
 }
 
@@ -932,7 +952,7 @@ void launch_gather(int modality, const TileDev &t, int64_t p0, int64_t np, const
 
 void launch_emb1(int C, const float *rec, int64_t M, const float *w1t, const float *b1, bf16 *y, cudaStream_t st) {
     if (M <= 0) return;
-    const unsigned grid = (unsigned)std::min<int64_t>(blocks_for(M, 8), 148 * 8);
+    const unsigned grid = (unsigned)std::min<int64_t>(blocks_for(M, 16), 148 * 8);
     if (C == 10) k_emb1<10><<<grid, 256, 0, st>>>(rec, M, w1t, b1, y);
     else if (C == 2) k_emb1<2><<<grid, 256, 0, st>>>(rec, M, w1t, b1, y);
     else throw std::runtime_error("emb1: unsupported band count");
