@@ -227,7 +227,7 @@ __device__ __forceinline__ void cp_async_wait_all() {
 //   O = bf16(P V) in two 80-column halves to bound register use
 // (tessera_cpu.cpp:333-343: matmul + linear post-op, softmax_accurate, matmul).
 template <int NTMAX>
-__global__ void __launch_bounds__(256, NTMAX <= 16 ? 2 : 1)
+__global__ void __launch_bounds__(NTMAX == 24 ? 512 : 256, NTMAX <= 16 ? 2 : 1)
     k_attention(const bf16 *__restrict__ qkv, Segs segs, bf16 *__restrict__ att, float scale) {
     extern __shared__ __align__(16) uint8_t att_smem[];
     const int64_t i = blockIdx.x;
@@ -1181,7 +1181,11 @@ template <int NT> static void attention_nt(const bf16 *qkv, Segs segs, int64_t n
         attr[dev & 63] = true;
     }
     const size_t smem = (size_t)2 * Tpad * ATT_LD * sizeof(bf16);
-    const int warps = std::min(8, Tpad / 16);
+    // Past 128 keys one CTA fills an SM's shared memory. Up to 192 keys it runs
+    // 16 warps, one per 16-row query block (T = 160: 440 against 517 us per
+    // 131k-token chunk with 8 warps); at 256 keys the 128-register cap of 16
+    // warps spills, so 8 warps stay.
+    const int warps = std::min(NT == 24 ? 16 : 8, Tpad / 16);
     const dim3 grid((unsigned)npix, NH);
     k_attention<NT><<<grid, 32 * warps, smem, st>>>(qkv, segs, att, 1.f / std::sqrt((float)HD));
 }
