@@ -399,7 +399,7 @@ def main():
         "warmup": args.warmup, "ms_per_step": dev_ms_max / args.steps, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": WORKLOAD if args.config == 1 else f"config {args.config}",
-                   "chunk_tokens": int(os.environ.get("TC_CHUNK_TOKENS", "131072")),
+                   "chunk_tokens": int(os.environ.get("TC_CHUNK_TOKENS", "524288")),
                    "pixels": total_px, "split": f"rows FLOP-balanced over {world} GPU(s)",
                    "weights": "Large, Xavier-uniform seed 0, zero biases",
                    "l2": "inputs (2.2 GB tile) larger than L2; no flush"},
