@@ -74,7 +74,9 @@ struct Blob {
     size_t put_bf16(const std::vector<float> &v) {
         const size_t o = reserve(v.size() * 2);
         uint16_t *d = reinterpret_cast<uint16_t *>(bytes.data() + o);
-        for (size_t i = 0; i < v.size(); ++i) d[i] = f2bf(v[i]);
+        const int64_t n = (int64_t)v.size();
+#pragma omp parallel for schedule(static) if (n > (1 << 16))
+        for (int64_t i = 0; i < n; ++i) d[i] = f2bf(v[i]);
         return o;
     }
 };
@@ -116,6 +118,7 @@ static void build_backbone(Blob &b, WeightMap &W, BackboneOff &o, const std::str
 }
 
 static void build_model(Blob &b, WeightMap &W, ModelOff &m) {
+    b.bytes.reserve(size_t(96) << 20);  // 88 MB of bf16 matrices plus f32 vectors and tables: no regrowth copies
     build_backbone(b, W, m.bb[0], "s2_backbone", 10);
     build_backbone(b, W, m.bb[1], "s1_backbone", 2);
     m.red1 = put_linear(b, W, "dim_reducer.0.weight", "dim_reducer.0.bias");

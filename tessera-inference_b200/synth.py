@@ -14,33 +14,11 @@ available, so tests and benchmarks use:
 """
 from __future__ import annotations
 
-import struct
 from pathlib import Path
 
 import numpy as np
 
-D, FF, NL, RED, OUT = 640, 2560, 4, 2560, 128
-
-
-def weight_shapes() -> list[tuple[str, tuple[int, ...]]]:
-    """Every tensor the Large student's C++ back ends read (tessera_cpu.cpp:459-502)."""
-    out = []
-    for pre, c in (("s2_backbone", 10), ("s1_backbone", 2)):
-        out += [(f"{pre}.embedding.0.weight", (D, c)), (f"{pre}.embedding.0.bias", (D,)),
-                (f"{pre}.embedding.2.weight", (D, D)), (f"{pre}.embedding.2.bias", (D,))]
-        for l in range(NL):
-            L = f"{pre}.transformer_encoder.layers.{l}"
-            out += [(f"{L}.self_attn.in_proj_weight", (3 * D, D)), (f"{L}.self_attn.in_proj_bias", (3 * D,)),
-                    (f"{L}.self_attn.out_proj.weight", (D, D)), (f"{L}.self_attn.out_proj.bias", (D,)),
-                    (f"{L}.linear1.weight", (FF, D)), (f"{L}.linear1.bias", (FF,)),
-                    (f"{L}.linear2.weight", (D, FF)), (f"{L}.linear2.bias", (D,)),
-                    (f"{L}.norm1.weight", (D,)), (f"{L}.norm1.bias", (D,)),
-                    (f"{L}.norm2.weight", (D,)), (f"{L}.norm2.bias", (D,))]
-        out += [(f"{pre}.attn_pool.query.weight", (1, D)), (f"{pre}.attn_pool.query.bias", (1,))]
-    out += [("dim_reducer.0.weight", (RED, 2 * D)), ("dim_reducer.0.bias", (RED,)),
-            ("dim_reducer.1.weight", (RED,)), ("dim_reducer.1.bias", (RED,)),
-            ("dim_reducer.4.weight", (OUT, RED)), ("dim_reducer.4.bias", (OUT,))]
-    return out
+from tcw import read_tcw, weight_shapes, write_tcw  # noqa: F401  (re-exported for tests)
 
 
 def random_weights(seed: int = 0, perturb: float = 0.0) -> dict[str, np.ndarray]:
@@ -68,32 +46,22 @@ def random_weights(seed: int = 0, perturb: float = 0.0) -> dict[str, np.ndarray]
     return w
 
 
-def write_tcw(path: Path | str, w: dict[str, np.ndarray]) -> None:
-    with open(path, "wb") as f:
-        f.write(b"TCW1")
-        f.write(struct.pack("<I", len(w)))
-        for k, v in w.items():
-            v = np.ascontiguousarray(v, dtype=np.float32)
-            f.write(struct.pack("<I", len(k)))
-            f.write(k.encode())
-            f.write(struct.pack("<I", v.ndim))
-            f.write(struct.pack(f"<{v.ndim}q", *v.shape))
-            f.write(v.tobytes())
-
-
-def read_tcw(path: Path | str) -> dict[str, np.ndarray]:
-    data = Path(path).read_bytes()
-    assert data[:4] == b"TCW1", "bad weights file"
-    (n,) = struct.unpack_from("<I", data, 4)
-    o, w = 8, {}
-    for _ in range(n):
-        (ln,) = struct.unpack_from("<I", data, o); o += 4
-        name = data[o:o + ln].decode(); o += ln
-        (nd,) = struct.unpack_from("<I", data, o); o += 4
-        shape = struct.unpack_from(f"<{nd}q", data, o); o += 8 * nd
-        cnt = int(np.prod(shape)) if nd else 1
-        w[name] = np.frombuffer(data, np.float32, cnt, o).reshape(shape); o += 4 * cnt
-    return w
+def fake_checkpoint(seed: int = 7, dtype: str = "float32", extra: bool = True) -> dict:
+    """A stand-in for the training checkpoint that tools/export_weights.py
+    reads: {"model": state dict of torch tensors, "args": the Large student's
+    sizes}. Values are random_weights(seed, perturb=0.1) in the given torch
+    dtype; extra=True adds two tensors the back ends do not read."""
+    import torch
+    sd = {k: torch.from_numpy(np.array(v)).to(getattr(torch, dtype))
+          for k, v in random_weights(seed, perturb=0.1).items()}
+    if extra:
+        rng = np.random.default_rng(seed + 1)
+        sd["s2_backbone.extra_head.weight"] = torch.from_numpy(rng.standard_normal((3, 5)).astype(np.float32)).to(
+            getattr(torch, dtype))
+        sd["step_count"] = torch.tensor([12345.0])
+    args = {"latent_dim": 160, "num_layers": 4, "nhead": 4, "dim_feedforward": 2560, "repr_dim": 128,
+            "enable_qk_norm": False, "lr": 1e-4}
+    return {"model": sd, "args": args}
 
 
 def make_weights(path: Path | str, seed: int = 0, perturb: float = 0.0) -> Path:

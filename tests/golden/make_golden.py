@@ -10,6 +10,10 @@
       (per tc_encode call: G, T2, T1 and sha256 of the s2 / s1 records the
       reference driver prepared) and <case>_oracle.npz (the codes and scales
       it wrote).
+  python tests/golden/make_golden.py export
+      export_ref.json: for synth.fake_checkpoint in f32 and in bf16, the
+      sha256 and size of the .tcw that the reference's unmodified
+      tools/export_weights.py writes (run here, from the reference tree).
   python tests/golden/make_golden.py refcuda       (on a B200)
       Runs the reference's unmodified driver + CUDA back end
       (oracle/_ref/tessera_encode_cuda_ref, built by `make -C oracle cuda-ref`)
@@ -152,11 +156,31 @@ def refcuda():
             print(name, codes.shape)
 
 
+def export():
+    import torch
+    script = Path(os.environ.get("REFERENCE_ROOT", "/root/reference")) / "tools" / "export_weights.py"
+    if not script.exists():
+        sys.exit(f"the reference's exporter is needed: {script}")
+    res = {}
+    with tempfile.TemporaryDirectory() as td:
+        for dtype in ("float32", "bfloat16"):
+            ck = Path(td) / f"ck_{dtype}.pt"
+            torch.save(synth.fake_checkpoint(7, dtype), ck)
+            out = Path(td) / f"ref_{dtype}.tcw"
+            subprocess.run([sys.executable, str(script), str(ck), str(out)], check=True)
+            data = out.read_bytes()
+            res[dtype] = {"sha256": hashlib.sha256(data).hexdigest(), "bytes": len(data)}
+    (HERE / "export_ref.json").write_text(json.dumps(res, indent=1) + "\n")
+    print(res)
+
+
 if __name__ == "__main__":
     cmd = sys.argv[1] if len(sys.argv) > 1 else "all"
     if cmd in ("padpattern", "all"):
         padpattern()
     if cmd in ("driver", "all"):
         driver()
+    if cmd in ("export", "all"):
+        export()
     if cmd == "refcuda":
         refcuda()
