@@ -379,78 +379,71 @@ __global__ void __launch_bounds__(NTMAX == 24 ? 512 : 256, NTMAX <= 16 ? 2 : 1)
 
 // ------------------------------------------------------------------ attention on tcgen05
 // Persistent, one CTA per SM, over (pixel, head) items with T <= 128 keys.
-//   warp 0       TMA (lane 0 K, lane 1 V): the item's K and V rows (boxes of
-//                32 rows x 64 columns, 128-byte swizzle, three 64-column slabs
-//                per matrix covering the head's 160 columns), each into one of
-//                two stages of its own; a K stage is released once S has read
-//                it, a V stage once O has.
+//   warp 0       TMA, boxes of 32 rows x 64 columns with 128-byte swizzle,
+//                three 64-column slabs per matrix covering the head's 160
+//                columns. Lane 0: the item's Q and K rows into the one Q/K
+//                stage, released once S has read it; lane 1: its V rows into
+//                one of two V stages, each released once O has read it.
 //   warp 1       TMEM allocation and MMA issue (one thread):
-//                  S = Q K^T   A = Q from TMEM, B = K (K-major), M = 128, N = Tpad
+//                  S = Q K^T   A = Q, B = K (both K-major in shared memory), M = 128, N = Tpad
 //                  O = P V     A = P from TMEM, B = V (MN-major), M = 128, N = 160
 //                S of the next item is issued before O of this one, so it runs
-//                while this item's softmax does.
+//                while this item's softmax does; the Q/K rows of the item after
+//                that load meanwhile.
 //   warps 2-17   softmax: four warps per TMEM lane quadrant, one query row per
 //                lane and 32 of the 128 key columns per warp. s = bf16(scale *
 //                S) and the row max, e = exp(s - max) and the row sum, then
 //                P = bf16(e / sum) over the T real keys back into TMEM. The
 //                four partial maxima and sums of a row meet in shared memory
-//                (one named barrier per quadrant). Each thread also writes 32
-//                columns of the next item's Q row to TMEM once this item's S is
-//                done, from registers loaded an item earlier.
-//   warps 18-21  O rows -> bf16 -> att, and the last 32 columns of each Q row.
-// Tensor memory (512 columns): Q [0, 80) as bf16 pairs, two S/P buffers
-// [96, 224) and [224, 352) (P overwrites the first Tpad/2 columns of its S),
-// O [352, 512).
+//                (one named barrier per quadrant).
+//   warps 18-21  O rows -> bf16 -> att: 32 columns at a time through a 2 KB
+//                staging buffer per warp, so that each store instruction
+//                writes 8 rows x 64 contiguous bytes.
+// Tensor memory (512 columns): two S/P buffers [96, 224) and [224, 352) (P
+// overwrites the first Tpad/2 columns of its S), O [352, 512).
 // Rows of K/V past T (up to the next multiple of 32) belong to the next pixel
 // or are zero-filled past the chunk; S columns >= T are masked and P is 0
-// there, so they never reach O. Query rows >= T are zero and not stored.
+// there, so they never reach O. Rows of S, P and O >= T come from rows of Q
+// that are not this item's and are never stored.
 // Every mbarrier wait is bounded.
 constexpr int AT_SLAB = 128 * 128;          // 128 rows x 64 bf16 = 16 KB
-constexpr int AT_STAGE = 6 * AT_SLAB;       // K and V, three slabs each
+constexpr int AT_MAT = 3 * AT_SLAB;         // one matrix: three slabs
+constexpr int AT_QK = 2 * AT_MAT;           // the Q/K stage
 constexpr int AT_SOFT_WARPS = 16, AT_IO_WARP0 = 2 + AT_SOFT_WARPS;
 constexpr int AT_THREADS = 32 * (AT_IO_WARP0 + 4);
 constexpr int AT_RED_BYTES = 2 * 4 * 128 * 4;  // partial max and sum: [slice][row] floats
-constexpr int AT_SMEM = 1024 + 2 * AT_STAGE + AT_RED_BYTES + 256;
-constexpr uint32_t AT_QCOL = 0, AT_SCOL0 = 96, AT_SCOL1 = 224, AT_OCOL = 352;
-
-// Write 16 TMEM columns (32 bf16 of Q) of this thread's lane, then arrive on q_full.
-__device__ __forceinline__ void store_q_chunk(uint32_t taddr, const uint4 (&q)[4], uint64_t *q_full, int lane) {
-    const uint32_t w[16] = {q[0].x, q[0].y, q[0].z, q[0].w, q[1].x, q[1].y, q[1].z, q[1].w,
-                            q[2].x, q[2].y, q[2].z, q[2].w, q[3].x, q[3].y, q[3].z, q[3].w};
-    tmem_st16(taddr, w);
-    tmem_st_wait();
-    tc_fence_before();
-    __syncwarp();
-    if (lane == 0) mbar_arrive(q_full);
-}
+constexpr int AT_OSTAGE = 2048;                // per O warp: 32 rows x 64 bytes
+constexpr int AT_RED_OFF = AT_QK + 2 * AT_MAT, AT_OST_OFF = AT_RED_OFF + AT_RED_BYTES,
+              AT_BAR_OFF = AT_OST_OFF + 4 * AT_OSTAGE;
+constexpr int AT_SMEM = 1024 + AT_BAR_OFF + 256;
+constexpr uint32_t AT_SCOL0 = 96, AT_SCOL1 = 224, AT_OCOL = 352;
 
 __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
 __global__ void __launch_bounds__(AT_THREADS, 1)
-    k_attention_tc(const __grid_constant__ CUtensorMap tm, Segs segs, int64_t nitems, const bf16 *__restrict__ qkv,
-                   bf16 *__restrict__ att, float scale, int *status) {
+    k_attention_tc(const __grid_constant__ CUtensorMap tm, Segs segs, int64_t nitems, bf16 *__restrict__ att,
+                   float scale, int *status) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    float *red_max = reinterpret_cast<float *>(smem + 2 * AT_STAGE), *red_sum = red_max + 4 * 128;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + 2 * AT_STAGE + AT_RED_BYTES);
-    uint64_t *k_full = bars, *k_empty = bars + 2, *v_full = bars + 4, *v_empty = bars + 6;
-    uint64_t *s_full = bars + 8, *p_full = bars + 10, *q_full = bars + 12, *o_full = bars + 13, *o_free = bars + 14;
-    uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 15);
+    float *red_max = reinterpret_cast<float *>(smem + AT_RED_OFF), *red_sum = red_max + 4 * 128;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + AT_BAR_OFF);
+    uint64_t *qk_full = bars, *qk_empty = bars + 1, *v_full = bars + 2, *v_empty = bars + 4;
+    uint64_t *s_full = bars + 6, *p_full = bars + 8, *o_full = bars + 10, *o_free = bars + 11;
+    uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 12);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     if (threadIdx.x == 0) {
+        mbar_init(qk_full, 1);
+        mbar_init(qk_empty, 1);
         for (int i = 0; i < 2; ++i) {
-            mbar_init(&k_full[i], 1);
-            mbar_init(&k_empty[i], 1);
             mbar_init(&v_full[i], 1);
             mbar_init(&v_empty[i], 1);
             mbar_init(&s_full[i], 1);
             mbar_init(&p_full[i], AT_SOFT_WARPS);
         }
-        mbar_init(q_full, AT_SOFT_WARPS + 4);
         mbar_init(o_full, 1);
         mbar_init(o_free, 4);
         *abort_flag = 0;
@@ -480,30 +473,63 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         }
         return it;
     };
+    // The offsets of a candidate item, loaded before a barrier wait so that
+    // their round trip overlaps the wait.
+    struct Pf { int64_t a = 0, b = 0; };
+    auto pf_load = [&](int64_t it) {
+        Pf f;
+        if (segs.off && it < nitems) {
+            const int64_t p = it >> 2;
+            f.a = segs.off[p];
+            f.b = segs.off[p + 1];
+        }
+        return f;
+    };
+    // next_item(it, ...) for a candidate whose offsets pf_load(it) fetched
+    auto next_item_pf = [&](int64_t it, const Pf &f, int64_t &t0, int &T, int &h) -> int64_t {
+        if (it >= nitems || !segs.off) return next_item(it, t0, T, h);
+        h = (int)(it & 3);
+        t0 = f.a - segs.base;
+        const int64_t len = f.b - f.a;
+        T = len > 128 ? 0 : (int)len;
+        return T > 0 ? it : next_item(it + gridDim.x, t0, T, h);
+    };
 
     if (warp == 0) {
-        if (lane < 2) {  // lane 0 loads K, lane 1 loads V
-            const int col0 = (lane == 0 ? D : 2 * D);
-            uint64_t *full = lane == 0 ? k_full : v_full, *empty = lane == 0 ? k_empty : v_empty;
-            const int off = lane == 0 ? 0 : 3 * AT_SLAB;
+        if (lane < 2) {  // lane 0 loads Q and K, lane 1 loads V
             int j = 0;
             int64_t t0;
             int T, h;
             for (int64_t it = next_item(blockIdx.x, t0, T, h); it < nitems; it = next_item(it + gridDim.x, t0, T, h)) {
-                const int s = j & 1;
-                if (!mbar_wait(&empty[s], ((j >> 1) & 1) ^ 1, abort_flag, status, ERR_WAIT_SMEM_EMPTY)) break;
                 const int nb = (T + 31) >> 5;
-                mbar_arrive_expect_tx(&full[s], (uint32_t)(nb * 3 * 32 * 128));
-                uint8_t *dst = smem + s * AT_STAGE + off;
-                for (int rb = 0; rb < nb; ++rb)
-                    for (int sl = 0; sl < 3; ++sl)
-                        tma_load_2d(dst + sl * AT_SLAB + rb * 4096, &tm, col0 + h * HD + sl * 64, (int)t0 + rb * 32,
-                                    &full[s]);
+                if (lane == 0) {
+                    if (!mbar_wait(qk_empty, (j & 1) ^ 1, abort_flag, status, ERR_WAIT_SMEM_EMPTY)) break;
+                    mbar_arrive_expect_tx(qk_full, (uint32_t)(nb * 2 * 3 * 32 * 128));
+                    for (int rb = 0; rb < nb; ++rb)
+                        for (int sl = 0; sl < 3; ++sl) {
+                            tma_load_2d(smem + sl * AT_SLAB + rb * 4096, &tm, h * HD + sl * 64, (int)t0 + rb * 32, qk_full);
+                            tma_load_2d(smem + AT_MAT + sl * AT_SLAB + rb * 4096, &tm, D + h * HD + sl * 64,
+                                        (int)t0 + rb * 32, qk_full);
+                        }
+                } else {
+                    const int s = j & 1;
+                    if (!mbar_wait(&v_empty[s], ((j >> 1) & 1) ^ 1, abort_flag, status, ERR_WAIT_SMEM_EMPTY)) break;
+                    mbar_arrive_expect_tx(&v_full[s], (uint32_t)(nb * 3 * 32 * 128));
+                    uint8_t *dst = smem + AT_QK + s * AT_MAT;
+                    for (int rb = 0; rb < nb; ++rb)
+                        for (int sl = 0; sl < 3; ++sl)
+                            tma_load_2d(dst + sl * AT_SLAB + rb * 4096, &tm, 2 * D + h * HD + sl * 64, (int)t0 + rb * 32,
+                                        &v_full[s]);
+                }
                 ++j;
             }
-            // both stages released: no MMA still reads shared memory at exit
-            for (int q = 0; q < 2; ++q, ++j)
-                if (!mbar_wait(&empty[j & 1], ((j >> 1) & 1) ^ 1, abort_flag, status, ERR_WAIT_SMEM_EMPTY)) break;
+            // every stage released: no MMA still reads shared memory at exit
+            if (lane == 0) {
+                mbar_wait(qk_empty, (j & 1) ^ 1, abort_flag, status, ERR_WAIT_SMEM_EMPTY);
+            } else {
+                for (int q = 0; q < 2; ++q, ++j)
+                    if (!mbar_wait(&v_empty[j & 1], ((j >> 1) & 1) ^ 1, abort_flag, status, ERR_WAIT_SMEM_EMPTY)) break;
+            }
         }
     } else if (warp == 1) {
         if (lane == 0) {
@@ -517,7 +543,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
                 if (!mbar_wait(o_free, (jj & 1) ^ 1, abort_flag, status, ERR_WAIT_TMEM_EMPTY)) return false;
                 tc_fence_after();
                 const uint32_t pcol = b ? AT_SCOL1 : AT_SCOL0;
-                const uint32_t sv = smem_u32(smem + b * AT_STAGE + 3 * AT_SLAB);
+                const uint32_t sv = smem_u32(smem + AT_QK + b * AT_MAT);
                 for (int k = 0; k < tpad / 16; ++k)
                     umma_bf16_tmem_a(tb + AT_OCOL, tb + pcol + (uint32_t)(k * 8),
                                      umma_desc_sw128_mn(sv + (uint32_t)(k * 16 * 128), AT_SLAB), idesc_o, k > 0);
@@ -525,26 +551,26 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
                 umma_commit(&v_empty[b]);
                 return true;
             };
+            const uint32_t sq = smem_u32(smem), sk = smem_u32(smem + AT_MAT);
             int64_t t0;
             int T, h;
             for (int64_t it = next_item(blockIdx.x, t0, T, h); it < nitems; it = next_item(it + gridDim.x, t0, T, h)) {
                 const int b = j & 1, tpad = (T + 15) & ~15;
                 // S(j)
-                if (!mbar_wait(&k_full[b], (j >> 1) & 1, abort_flag, status, ERR_WAIT_TMA_FULL)) { ok = false; break; }
-                if (!mbar_wait(q_full, j & 1, abort_flag, status, ERR_WAIT_TMEM_FULL)) { ok = false; break; }
+                if (!mbar_wait(qk_full, j & 1, abort_flag, status, ERR_WAIT_TMA_FULL)) { ok = false; break; }
                 // S(j) overwrites the S/P buffer of item j - 2: its O must be complete
                 if (!mbar_wait(&v_empty[b], ((j >> 1) & 1) ^ 1, abort_flag, status, ERR_WAIT_TMEM_EMPTY)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t scol = b ? AT_SCOL1 : AT_SCOL0;
-                const uint32_t sk = smem_u32(smem + b * AT_STAGE);
                 const uint32_t idesc_s = umma_idesc_bf16(128, tpad);
 #pragma unroll
-                for (int k = 0; k < HD / 16; ++k)
-                    umma_bf16_tmem_a(tb + scol, tb + AT_QCOL + (uint32_t)(k * 8),
-                                     umma_desc_sw128(sk + (uint32_t)((k >> 2) * AT_SLAB)) + (uint64_t)(2 * (k & 3)),
-                                     idesc_s, k > 0);
+                for (int k = 0; k < HD / 16; ++k) {
+                    const uint32_t slab = (uint32_t)((k >> 2) * AT_SLAB);
+                    umma_bf16(tb + scol, umma_desc_sw128(sq + slab) + (uint64_t)(2 * (k & 3)),
+                              umma_desc_sw128(sk + slab) + (uint64_t)(2 * (k & 3)), idesc_s, k > 0);
+                }
                 umma_commit(&s_full[b]);
-                umma_commit(&k_empty[b]);
+                umma_commit(qk_empty);
                 // O(j - 1)
                 if (j > 0 && !issue_pv(j - 1, prev_tpad)) { ok = false; break; }
                 prev_tpad = tpad;
@@ -556,43 +582,20 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         // softmax: quadrant = warp % 4 (the TMEM lanes this warp may access), 32-column slice
         const int quad = warp & 3, slice = (warp - 2) >> 2, r = quad * 32 + lane, c0 = slice * 32;
         const uint32_t lanebits = (uint32_t)(quad * 32) << 16;
-        // Q row r as 5 chunks of 32 bf16 (16 TMEM columns each): slice s writes
-        // chunk s, the O warps chunk 4
-        uint4 qv[4];
-        auto load_q = [&](int64_t q0, int qT, int qh) {
-            const uint4 *src = reinterpret_cast<const uint4 *>(qkv + (q0 + r) * (3 * D) + qh * HD) + slice * 4;
-#pragma unroll
-            for (int c = 0; c < 4; ++c) qv[c] = r < qT ? src[c] : make_uint4(0, 0, 0, 0);
-        };
-        auto store_q = [&]() { store_q_chunk(tb + lanebits + AT_QCOL + (uint32_t)(slice * 16), qv, q_full, lane); };
-        // Q runs two items ahead: Q(j + 1) is written once S(j) is done, and
-        // the loads of Q(j + 2) are issued right after.
         int j = 0;
-        int64_t t0, t0n = 0;
-        int T, h, Tn = 0, hn = 0;
+        int64_t t0;
+        int T, h;
         int64_t it = next_item(blockIdx.x, t0, T, h);
-        if (it < nitems) {
-            load_q(t0, T, h);
-            store_q();
-        }
-        int64_t it2 = it < nitems ? next_item(it + gridDim.x, t0n, Tn, hn) : nitems;
-        if (it2 < nitems) load_q(t0n, Tn, hn);
         while (it < nitems) {
             const int b = j & 1, tpad = (T + 15) & ~15;
             const uint32_t scol = (b ? AT_SCOL1 : AT_SCOL0) + (uint32_t)c0;
+            const Pf pfn = pf_load(it + gridDim.x);
             if (!mbar_wait(&s_full[b], (j >> 1) & 1, abort_flag, status, ERR_WAIT_TMEM_FULL)) break;
             tc_fence_after();
             uint32_t v[2][16];  // 32 columns of the S row, then s, then e, as f32 bits
             if (c0 < tpad) tmem_ld16(tb + lanebits + scol, v[0]);
             if (c0 + 16 < tpad) tmem_ld16(tb + lanebits + scol + 16, v[1]);
             tmem_ld_wait();
-            int64_t t0nn = 0;
-            int Tnn = 0, hnn = 0;
-            const int64_t it3 = it2 < nitems ? next_item(it2 + gridDim.x, t0nn, Tnn, hnn) : nitems;
-            if (it2 < nitems) {
-                store_q();  // S(j) has consumed Q(j)
-                if (it3 < nitems) load_q(t0nn, Tnn, hnn);
-            }
             // 16-column halves past Tpad are skipped (the branch is uniform per warp)
             float mx = -INFINITY;
 #pragma unroll
@@ -637,78 +640,58 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&p_full[b]);
-            it = it2;
-            t0 = t0n;
-            T = Tn;
-            h = hn;
-            it2 = it3;
-            t0n = t0nn;
-            Tn = Tnn;
-            hn = hnn;
+            it = next_item_pf(it + gridDim.x, pfn, t0, T, h);
             ++j;
         }
     } else {
-        // O warps, which also write chunk 4 of each Q row
-        const int quad = warp & 3, r = quad * 32 + lane;
+        // O warps: each drains its TMEM lane quadrant (32 query rows) of O(j)
+        const int quad = warp & 3;
         const uint32_t lanebits = (uint32_t)(quad * 32) << 16;
-        uint4 qv[4];
-        auto load_q = [&](int64_t q0, int qT, int qh) {
-            const uint4 *src = reinterpret_cast<const uint4 *>(qkv + (q0 + r) * (3 * D) + qh * HD) + 16;
-#pragma unroll
-            for (int c = 0; c < 4; ++c) qv[c] = r < qT ? src[c] : make_uint4(0, 0, 0, 0);
-        };
-        auto store_q = [&]() { store_q_chunk(tb + lanebits + AT_QCOL + 64, qv, q_full, lane); };
+        uint8_t *stage = smem + AT_OST_OFF + (warp - AT_IO_WARP0) * AT_OSTAGE;
+        uint4 *my_row = reinterpret_cast<uint4 *>(stage + lane * 64);
+        const int sw = (lane >> 1) & 3;
         int j = 0;
-        int64_t t0, t0n = 0;
-        int T, h, Tn = 0, hn = 0;
+        int64_t t0;
+        int T, h;
         int64_t it = next_item(blockIdx.x, t0, T, h);
-        if (it < nitems) {
-            load_q(t0, T, h);
-            store_q();
-        }
-        int64_t it2 = it < nitems ? next_item(it + gridDim.x, t0n, Tn, hn) : nitems;
-        if (it2 < nitems) load_q(t0n, Tn, hn);
         while (it < nitems) {
-            if (!mbar_wait(&s_full[j & 1], (j >> 1) & 1, abort_flag, status, ERR_WAIT_TMEM_FULL)) break;
-            tc_fence_after();
-            int64_t t0nn = 0;
-            int Tnn = 0, hnn = 0;
-            const int64_t it3 = it2 < nitems ? next_item(it2 + gridDim.x, t0nn, Tnn, hnn) : nitems;
-            if (it2 < nitems) {
-                store_q();  // S(j) has consumed Q(j)
-                if (it3 < nitems) load_q(t0nn, Tnn, hnn);
-            }
+            const Pf pfn = pf_load(it + gridDim.x);
             if (!mbar_wait(o_full, j & 1, abort_flag, status, ERR_WAIT_TMEM_FULL)) break;
             tc_fence_after();
-            uint4 *dst = reinterpret_cast<uint4 *>(att + (t0 + r) * D + h * HD);
-#pragma unroll
-            for (int c = 0; c < HD / 32; ++c) {
-                uint32_t v[16], w[16];
-                tmem_ld16(tb + lanebits + AT_OCOL + (uint32_t)(c * 32), v);
-                tmem_ld16(tb + lanebits + AT_OCOL + (uint32_t)(c * 32 + 16), w);
-                tmem_ld_wait();
-                if (r < T) {
+            const int nrows = T - quad * 32;  // real rows of this quadrant (uniform per warp)
+            if (nrows > 0) {
+                bf16 *dst = att + (t0 + quad * 32) * D + h * HD;
+#pragma unroll 1
+                for (int c = 0; c < HD / 32; ++c) {
+                    uint32_t v[16], w[16];
+                    tmem_ld16(tb + lanebits + AT_OCOL + (uint32_t)(c * 32), v);
+                    tmem_ld16(tb + lanebits + AT_OCOL + (uint32_t)(c * 32 + 16), w);
+                    tmem_ld_wait();
                     uint32_t o[16];
 #pragma unroll
                     for (int k = 0; k < 8; ++k) {
                         o[k] = pack_bf16x2(__uint_as_float(v[2 * k]), __uint_as_float(v[2 * k + 1]));
                         o[8 + k] = pack_bf16x2(__uint_as_float(w[2 * k]), __uint_as_float(w[2 * k + 1]));
                     }
+                    // row-per-lane into the staging rows (16-byte chunks XOR-swizzled
+                    // so the writes and the row-wise reads are conflict-free), then
+                    // 8 rows x 64 bytes per store instruction
 #pragma unroll
-                    for (int k = 0; k < 4; ++k) dst[c * 4 + k] = make_uint4(o[4 * k], o[4 * k + 1], o[4 * k + 2], o[4 * k + 3]);
+                    for (int k = 0; k < 4; ++k) my_row[k ^ sw] = make_uint4(o[4 * k], o[4 * k + 1], o[4 * k + 2], o[4 * k + 3]);
+                    __syncwarp();
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const int rr = i * 8 + (lane >> 2), k = lane & 3;
+                        const uint4 val = reinterpret_cast<const uint4 *>(stage + rr * 64)[k ^ ((rr >> 1) & 3)];
+                        if (rr < nrows) *reinterpret_cast<uint4 *>(dst + (int64_t)rr * D + c * 32 + k * 8) = val;
+                    }
+                    __syncwarp();
                 }
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(o_free);
-            it = it2;
-            t0 = t0n;
-            T = Tn;
-            h = hn;
-            it2 = it3;
-            t0n = t0nn;
-            Tn = Tnn;
-            hn = hnn;
+            it = next_item_pf(it + gridDim.x, pfn, t0, T, h);
             ++j;
         }
     }
@@ -1218,16 +1201,16 @@ static int attention_tcgen05() {
 //   cost follows Tpad_max: 19, 38, 62, 89, 126, 179, 228, 266 ns at
 //   Tpad = 16, 32, ..., 128;
 // * the tcgen05 kernel pays a fixed cost per (pixel, head) item plus a little
-//   per key: about 35 + 1.3 * T_mean ns.
-// Uniform T = 80 stays on mma.sync (206 against 216 us per chunk), T = 96
-// moves to tcgen05 (205 against 244 us); a config-1 S2 chunk (T_mean ~ 72,
-// T_max ~ 104) goes to tcgen05 (225 against 260 us).
+//   per key: about 37.6 + 0.71 * T_mean ns (49 ns at T = 16, 128 ns at 128).
+// Uniform T = 48 stays on mma.sync (169 against 195 us per chunk), T = 64
+// moves to tcgen05 (165 against 183 us); a config-1 S2 chunk (T_mean ~ 72,
+// T_max ~ 104) goes to tcgen05 (168 against 260 us).
 static double attention_mma_cost_ns(int tpad) {
     static const double c[8] = {19, 38, 62, 89, 126, 179, 228, 266};
     const int i = std::min(std::max(tpad / 16, 1), 8) - 1;
     return c[i];
 }
-static double attention_tc_cost_ns(double t_mean) { return 35.0 + 1.3 * t_mean; }
+static double attention_tc_cost_ns(double t_mean) { return 37.6 + 0.71 * t_mean; }
 
 static void attention_tc(const bf16 *qkv, Segs segs, int64_t npix, int64_t ntok, bf16 *att, int *status,
                          cudaStream_t st) {
@@ -1246,7 +1229,7 @@ static void attention_tc(const bf16 *qkv, Segs segs, int64_t npix, int64_t ntok,
     make_tmap_box(&tm, qkv, (uint64_t)ntok, (uint64_t)(3 * D), (uint64_t)(3 * D), 64, 32, CU_TENSOR_MAP_SWIZZLE_128B);
     const int64_t items = npix * NH;
     const unsigned grid = (unsigned)std::min<int64_t>(items, grid_per_dev[dev & 63]);
-    k_attention_tc<<<grid, AT_THREADS, AT_SMEM, st>>>(tm, segs, items, qkv, att, 1.f / std::sqrt((float)HD), status);
+    k_attention_tc<<<grid, AT_THREADS, AT_SMEM, st>>>(tm, segs, items, att, 1.f / std::sqrt((float)HD), status);
 }
 
 void launch_attention(const bf16 *qkv, Segs segs, int64_t npix, int64_t ntok, int Tmax, bf16 *att, int *status,
