@@ -247,6 +247,7 @@ struct Dev {
     DevBuf<uint8_t> tile;  // band copy of the tile arrays
     DevBuf<int32_t> n2, n1, bins2, bins1;
     DevBuf<int64_t> off2, off1;
+    DevBuf<int32_t> list2, list1;  // per chunk, its pixels by attention class
     DevBuf<uint8_t> empty;
     DevBuf<int8_t> codes;
     DevBuf<float> scales;
@@ -266,6 +267,7 @@ struct Dev {
         rec.release(); y.release(); x.release(); x1.release(); att.release(); qkv.release(); hbuf.release();
         fused.release(); r1.release(); r2.release(); status.release(); in2.release(); in1.release(); outf.release();
         tile.release(); n2.release(); n1.release(); bins2.release(); bins1.release(); off2.release(); off1.release();
+        list2.release(); list1.release();
         empty.release(); codes.release(); scales.release(); hcnt.release(); hseg.release();
         if (wdev) cudaFree(wdev);
         if (own) cudaStreamDestroy(own);
@@ -377,7 +379,9 @@ static bool ln_fused() {
 }
 
 // One backbone over a chunk's token stream: records (M, C+1) -> fused[:, col0:col0+640].
-static void backbone(Dev &d, int b, const float *rec, Segs segs, int64_t M, int Tmax, int64_t npix) {
+// plan: the chunk's pixels by attention class; null when every series has length Tmax.
+static void backbone(Dev &d, int b, const float *rec, Segs segs, int64_t M, int Tmax, int64_t npix,
+                     const AttnPlan *plan = nullptr) {
     const BackboneDev &B = d.m.bb[b];
     if (M > d.tok_cap) throw std::runtime_error("chunk larger than the token workspace");
     if (M > 0) {
@@ -388,7 +392,8 @@ static void backbone(Dev &d, int b, const float *rec, Segs segs, int64_t M, int 
         for (int l = 0; l < NL; ++l) {
             gemm(d, GK_QKV, B.qkv[l], d.x.p, M, d.qkv.p, false);
             d.mark(TC_CAT_ATTN);
-            launch_attention(d.qkv.p, segs, npix, M, Tmax, d.att.p, d.status.p, d.st);
+            if (plan) launch_attention_plan(d.qkv.p, segs, *plan, M, d.att.p, d.status.p, d.st);
+            else launch_attention(d.qkv.p, segs, npix, M, Tmax, d.att.p, d.status.p, d.st);
             if (ln_fused()) {  // LN1 / LN2 in the epilogues of out-proj / FFN2
                 gemm(d, GK_OUT, B.out[l], d.att.p, M, d.x1.p, false, d.x.p, nullptr, 1, B.ln1g[l], B.ln1b[l]);
                 gemm(d, GK_FFN1, B.ffn1[l], d.x1.p, M, d.hbuf.p, true);
@@ -473,13 +478,15 @@ static void encode_band(Dev &d, const TileDev &t, int64_t p0, int64_t np, int8_t
     CK(cudaMemcpyAsync(d.hcnt.p + np, d.n1.p, np * 4, cudaMemcpyDeviceToHost, d.st));
     CK(cudaStreamSynchronize(d.st));
     // host: bins, per-pixel token counts, offsets, chunk plan
-    const size_t seg_bytes = (size_t)np * (4 + 4 + 1) + (size_t)(np + 1) * 16 + 64;
+    const size_t seg_bytes = (size_t)np * (4 + 4 + 1) + (size_t)(np + 1) * 16 + (size_t)np * 8 + 96;
     d.hseg.ensure(seg_bytes);
     int32_t *b2 = reinterpret_cast<int32_t *>(d.hseg.p);
     int32_t *b1 = b2 + np;
     int64_t *o2 = reinterpret_cast<int64_t *>(((uintptr_t)(b1 + np) + 15) & ~uintptr_t(15));
     int64_t *o1 = o2 + np + 1;
     uint8_t *em = reinterpret_cast<uint8_t *>(o1 + np + 1);
+    int32_t *l2 = reinterpret_cast<int32_t *>(((uintptr_t)(em + np) + 15) & ~uintptr_t(15));
+    int32_t *l1 = l2 + np;
     const int32_t *c2 = d.hcnt.p, *c1 = d.hcnt.p + np;
     o2[0] = o1[0] = 0;
     double flop = 0.0;
@@ -499,6 +506,10 @@ static void encode_band(Dev &d, const TileDev &t, int64_t p0, int64_t np, int8_t
     CK(cudaMemcpyAsync(d.off2.p, o2, (np + 1) * 8, cudaMemcpyHostToDevice, d.st));
     CK(cudaMemcpyAsync(d.off1.p, o1, (np + 1) * 8, cudaMemcpyHostToDevice, d.st));
     CK(cudaMemcpyAsync(d.empty.p, em, np, cudaMemcpyHostToDevice, d.st));
+    // chunks, and each chunk's pixels by attention class (list entries of the
+    // chunk [i0, i1) sit at [i0, i1), relative to i0)
+    struct ChunkPlan { int64_t i0, i1; int Tm2, Tm1; AttnPlan a2, a1; };
+    std::vector<ChunkPlan> chunks;
     for (int64_t i0 = 0; i0 < np;) {
         int64_t i1 = i0;
         int Tm2 = 0, Tm1 = 0;
@@ -508,17 +519,28 @@ static void encode_band(Dev &d, const TileDev &t, int64_t p0, int64_t np, int8_t
             ++i1;
         }
         if (i1 == i0) throw std::runtime_error("token workspace smaller than one pixel");
-        const int64_t n = i1 - i0;
+        ChunkPlan c{i0, i1, Tm2, Tm1, {}, {}};
+        attention_plan(o2 + i0, i1 - i0, l2 + i0, c.a2);
+        attention_plan(o1 + i0, i1 - i0, l1 + i0, c.a1);
+        chunks.push_back(c);
+        i0 = i1;
+    }
+    d.list2.ensure(np); d.list1.ensure(np);
+    CK(cudaMemcpyAsync(d.list2.p, l2, np * 4, cudaMemcpyHostToDevice, d.st));
+    CK(cudaMemcpyAsync(d.list1.p, l1, np * 4, cudaMemcpyHostToDevice, d.st));
+    for (ChunkPlan &c : chunks) {
+        const int64_t i0 = c.i0, i1 = c.i1, n = i1 - i0;
+        c.a2.pix = d.list2.p + i0;
+        c.a1.pix = d.list1.p + i0;
         const Segs s2{d.off2.p + i0, o2[i0], 0}, s1{d.off1.p + i0, o1[i0], 0};
         d.mark(TC_CAT_PREP);
         launch_gather(0, t, p0 + i0, n, nullptr, d.bins2.p + i0, s2, d.rec.p, d.st);
-        backbone(d, 0, d.rec.p, s2, o2[i1] - o2[i0], Tm2, n);
+        backbone(d, 0, d.rec.p, s2, o2[i1] - o2[i0], c.Tm2, n, &c.a2);
         d.mark(TC_CAT_PREP);
         launch_gather(1, t, p0 + i0, n, nullptr, d.bins1.p + i0, s1, d.rec.p, d.st);
-        backbone(d, 1, d.rec.p, s1, o1[i1] - o1[i0], Tm1, n);
+        backbone(d, 1, d.rec.p, s1, o1[i1] - o1[i0], c.Tm1, n, &c.a1);
         head(d, n, d.empty.p + i0, nullptr, codes + i0 * OUT, scales + i0);
         d.stats.launches += 2;
-        i0 = i1;
     }
     d.stats.pixels += double(np);
     d.stats.alg_flop += flop;
@@ -977,14 +999,40 @@ int tcb_op_emb1(int C, const float *rec, int64_t M, const float *w1t, const floa
     OP_TRY("tcb_op_emb1", launch_emb1(C, rec, M, w1t, b1, static_cast<bf16 *>(y), static_cast<cudaStream_t>(stream)))
 }
 
+namespace {
+struct DevFree {
+    void operator()(int32_t *p) const { cudaFree(p); }
+};
+using DevList = std::unique_ptr<int32_t, DevFree>;
+}  // namespace
+
 int tcb_op_attention(const void *qkv, const int64_t *off, int64_t uniform_T, int64_t npix, int Tmax, void *att,
                      void *stream) {
     OP_TRY("tcb_op_attention", {
-        // the qkv rows the segments reach: off[npix] (read back), or npix * uniform_T
-        int64_t ntok = npix * uniform_T;
-        if (off && npix > 0) CK(cudaMemcpy(&ntok, off + npix, sizeof(int64_t), cudaMemcpyDeviceToHost));
-        launch_attention(static_cast<const bf16 *>(qkv), Segs{off, 0, uniform_T}, npix, ntok, Tmax,
-                         static_cast<bf16 *>(att), nullptr, static_cast<cudaStream_t>(stream));
+        const cudaStream_t st = static_cast<cudaStream_t>(stream);
+        if (!off || npix <= 0) {
+            launch_attention(static_cast<const bf16 *>(qkv), Segs{nullptr, 0, uniform_T}, npix, npix * uniform_T,
+                             Tmax, static_cast<bf16 *>(att), nullptr, st);
+        } else {
+            // the offsets are read back to list the pixels by attention class, as
+            // the tile path does; the qkv rows the segments reach are off[npix]
+            std::vector<int64_t> ho((size_t)npix + 1);
+            std::vector<int32_t> list((size_t)npix);
+            CK(cudaMemcpyAsync(ho.data(), off, (npix + 1) * sizeof(int64_t), cudaMemcpyDeviceToHost, st));
+            CK(cudaStreamSynchronize(st));
+            for (int64_t i = 0; i < npix; ++i)
+                if (ho[i + 1] - ho[i] > Tmax) throw std::runtime_error("a segment is longer than Tmax");
+            AttnPlan plan;
+            attention_plan(ho.data(), npix, list.data(), plan);
+            int32_t *dl = nullptr;
+            CK(cudaMalloc(&dl, std::max<size_t>(list.size(), 1) * sizeof(int32_t)));
+            const DevList guard(dl);
+            CK(cudaMemcpyAsync(dl, list.data(), list.size() * sizeof(int32_t), cudaMemcpyHostToDevice, st));
+            plan.pix = dl;
+            launch_attention_plan(static_cast<const bf16 *>(qkv), Segs{off, 0, 0}, plan, ho[npix],
+                                  static_cast<bf16 *>(att), nullptr, st);
+            CK(cudaStreamSynchronize(st));
+        }
     })
 }
 

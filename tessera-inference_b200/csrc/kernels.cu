@@ -33,6 +33,8 @@ constexpr float Z_EPS = 1e-9f;
 __device__ __forceinline__ int64_t seg_at(const Segs &s, int64_t i) {
     return s.off ? s.off[i] - s.base : i * s.uniform_T;
 }
+// The chunk segment that segment k of an attention launch stands for.
+__device__ __forceinline__ int64_t seg_pix(const Segs &s, int64_t k) { return s.pix ? (int64_t)s.pix[k] : k; }
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
@@ -230,7 +232,7 @@ template <int NTMAX>
 __global__ void __launch_bounds__(NTMAX == 24 ? 512 : 256, NTMAX <= 16 ? 2 : 1)
     k_attention(const bf16 *__restrict__ qkv, Segs segs, bf16 *__restrict__ att, float scale) {
     extern __shared__ __align__(16) uint8_t att_smem[];
-    const int64_t i = blockIdx.x;
+    const int64_t i = seg_pix(segs, blockIdx.x);
     const int h = blockIdx.y;
     const int64_t t0 = seg_at(segs, i);
     const int T = (int)(seg_at(segs, i + 1) - t0);
@@ -459,7 +461,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     // series (a caller's Tmax below the real one) is skipped by all roles and
     // reported as a bad segment.
     auto item_at = [&](int64_t it, int64_t &t0, int &T, int &h) {
-        const int64_t p = it >> 2;
+        const int64_t p = seg_pix(segs, it >> 2);
         h = (int)(it & 3);
         t0 = seg_at(segs, p);
         const int64_t len = seg_at(segs, p + 1) - t0;
@@ -479,7 +481,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     auto pf_load = [&](int64_t it) {
         Pf f;
         if (segs.off && it < nitems) {
-            const int64_t p = it >> 2;
+            const int64_t p = seg_pix(segs, it >> 2);
             f.a = segs.off[p];
             f.b = segs.off[p + 1];
         }
@@ -1075,7 +1077,7 @@ __global__ void __launch_bounds__(256, 1)
     bf16 *buf_base = reinterpret_cast<bf16 *>(att_smem);          // [2 buffers][K, V][TP][ATT_LD]
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
     auto info = [&](int64_t it, int64_t &t0, int &T, int &h) {
-        const int64_t px = it >> 2;
+        const int64_t px = seg_pix(segs, it >> 2);
         h = (int)(it & 3);
         t0 = seg_at(segs, px);
         T = (int)(seg_at(segs, px + 1) - t0);
@@ -1195,22 +1197,12 @@ static int attention_tcgen05() {
     return mode;
 }
 
-// Kernel choice by cost per pixel (ns, all 4 heads), fitted to B200 timings
-// of 131,072-token chunks of uniform series length T:
-// * the mma.sync kernel sizes every CTA by the chunk's longest series, so its
-//   cost follows Tpad_max: 19, 38, 62, 89, 126, 179, 228, 266 ns at
-//   Tpad = 16, 32, ..., 128;
-// * the tcgen05 kernel pays a fixed cost per (pixel, head) item plus a little
-//   per key: about 37.6 + 0.71 * T_mean ns (49 ns at T = 16, 128 ns at 128).
-// Uniform T = 48 stays on mma.sync (169 against 195 us per chunk), T = 64
-// moves to tcgen05 (165 against 183 us); a config-1 S2 chunk (T_mean ~ 72,
-// T_max ~ 104) goes to tcgen05 (168 against 260 us).
-static double attention_mma_cost_ns(int tpad) {
-    static const double c[8] = {19, 38, 62, 89, 126, 179, 228, 266};
-    const int i = std::min(std::max(tpad / 16, 1), 8) - 1;
-    return c[i];
-}
-static double attention_tc_cost_ns(double t_mean) { return 37.6 + 0.71 * t_mean; }
+// Longest series left to the mma.sync kernel when both kernels are on. Timed
+// on B200 over 131,072-token chunks of uniform T (us per chunk, mma.sync /
+// tcgen05): T = 32: 156 / 243, T = 48: 169 / 195, T = 64: 183 / 165, T = 96:
+// 244 / 144, T = 128: 272 / 131. Bins are multiples of 8, so 48 is the last
+// length where mma.sync is faster.
+constexpr int AT_MMA_MAX_T = 48;
 
 static void attention_tc(const bf16 *qkv, Segs segs, int64_t npix, int64_t ntok, bf16 *att, int *status,
                          cudaStream_t st) {
@@ -1232,14 +1224,36 @@ static void attention_tc(const bf16 *qkv, Segs segs, int64_t npix, int64_t ntok,
     k_attention_tc<<<grid, AT_THREADS, AT_SMEM, st>>>(tm, segs, items, att, 1.f / std::sqrt((float)HD), status);
 }
 
-void launch_attention(const bf16 *qkv, Segs segs, int64_t npix, int64_t ntok, int Tmax, bf16 *att, int *status,
-                      cudaStream_t st) {
-    if (npix <= 0 || Tmax <= 0) return;
-    if (Tmax > 256) throw std::runtime_error("attention: T > 256");
-    const int Tpad = (Tmax + 15) & ~15;
-    const int tc_mode = attention_tcgen05();
-    const bool tc_cheaper = ntok > 0 && attention_tc_cost_ns(double(ntok) / double(npix)) < attention_mma_cost_ns(Tpad);
-    if (Tpad <= 128 && ntok > 0 && (tc_mode == 2 || (tc_mode == 1 && tc_cheaper)) && !attention_pipelined()) {
+int attention_class(int T) {
+    if (T > 128) return 2;
+    if (attention_pipelined()) return 0;
+    const int mode = attention_tcgen05();
+    return mode == 2 || (mode == 1 && T > AT_MMA_MAX_T) ? 1 : 0;
+}
+
+void attention_plan(const int64_t *off, int64_t npix, int32_t *list, AttnPlan &plan) {
+    plan = AttnPlan{};
+    for (int64_t i = 0; i < npix; ++i) {
+        const int64_t T = off[i + 1] - off[i];
+        if (T <= 0) continue;
+        const int c = attention_class((int)std::min<int64_t>(T, 1 << 30));
+        ++plan.n[c];
+        plan.tmax[c] = (int)std::max<int64_t>(plan.tmax[c], T);
+    }
+    int64_t pos[3] = {0, plan.n[0], plan.n[0] + plan.n[1]};
+    for (int64_t i = 0; i < npix; ++i) {
+        const int64_t T = off[i + 1] - off[i];
+        if (T > 0) list[pos[attention_class((int)std::min<int64_t>(T, 1 << 30))]++] = (int32_t)i;
+    }
+}
+
+// npix segments of one class (through segs.pix when set), the longest tmax.
+static void attention_of_class(int cls, const bf16 *qkv, Segs segs, int64_t npix, int64_t ntok, int tmax, bf16 *att,
+                               int *status, cudaStream_t st) {
+    if (npix <= 0 || tmax <= 0) return;
+    if (tmax > 256) throw std::runtime_error("attention: T > 256");
+    const int Tpad = (tmax + 15) & ~15;
+    if (cls == 1) {
         attention_tc(qkv, segs, npix, ntok, att, status, st);
     } else if (attention_pipelined()) {
         if (Tpad <= 32) attention_pipe<4>(qkv, segs, npix, att, st);
@@ -1257,6 +1271,24 @@ void launch_attention(const bf16 *qkv, Segs segs, int64_t npix, int64_t ntok, in
         else if (Tpad <= 192) attention_nt<24>(qkv, segs, npix, Tpad, att, st);
         else attention_nt<32>(qkv, segs, npix, Tpad, att, st);
     }
+}
+
+void launch_attention_plan(const bf16 *qkv, Segs segs, const AttnPlan &plan, int64_t ntok, bf16 *att, int *status,
+                           cudaStream_t st) {
+    int64_t o = 0;
+    for (int c = 0; c < 3; ++c) {
+        Segs s = segs;
+        s.pix = plan.pix + o;
+        attention_of_class(c, qkv, s, plan.n[c], ntok, plan.tmax[c], att, status, st);
+        o += plan.n[c];
+    }
+    check_launch("k_attention");
+}
+
+void launch_attention(const bf16 *qkv, Segs segs, int64_t npix, int64_t ntok, int Tmax, bf16 *att, int *status,
+                      cudaStream_t st) {
+    if (npix <= 0 || Tmax <= 0) return;
+    attention_of_class(attention_class(Tmax), qkv, segs, npix, ntok, Tmax, att, status, st);
     check_launch("k_attention");
 }
 

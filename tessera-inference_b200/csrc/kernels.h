@@ -15,6 +15,8 @@ struct Segs {
     const int64_t *off = nullptr;
     int64_t base = 0;
     int64_t uniform_T = 0;
+    // attention launches only: segment k of the launch is segment pix[k] of the chunk
+    const int32_t *pix = nullptr;
 };
 
 // Raw tile arrays in device memory (tessera_encode.cpp:182-209 layout).
@@ -45,10 +47,34 @@ void launch_gather(int modality, const TileDev &t, int64_t p0, int64_t np, const
 void launch_emb1(int C, const float *rec, int64_t M, const float *w1t, const float *b1, __nv_bfloat16 *y,
                  cudaStream_t st);
 
-// Self-attention of every pixel segment, 4 heads x 160, no mask (tessera_cpu.cpp:410-418).
-// qkv holds ntok token rows of 1920 (the rows the segments index). Series of
-// up to 128 steps run on the tcgen05 kernel, whose bounded waits report into
-// *status (may be null); longer ones on the mma.sync kernel.
+// Self-attention of pixel segments, 4 heads x 160, no mask (tessera_cpu.cpp:410-418).
+// qkv holds ntok token rows of 1920 (the rows the segments index).
+//
+// The kernel for a pixel is chosen by that pixel's own series length T, so a
+// pixel's result never depends on which other pixels share its chunk (row
+// bands, devices and the tc_encode batches all give the same bytes):
+//   class 0: the mma.sync kernel, for T <= 48 (every T <= 128 with TC_ATTN_TC=0
+//            or TC_ATTN_PIPE=1);
+//   class 1: the tcgen05 kernel, for 48 < T <= 128 (every T <= 128 with
+//            TC_ATTN_TC=2); its bounded waits report into *status (may be null);
+//   class 2: the mma.sync kernel, for T > 128.
+int attention_class(int T);
+
+// A chunk's pixels with T > 0 listed class by class (device memory), with the
+// count and the longest series of each class.
+struct AttnPlan {
+    const int32_t *pix = nullptr;
+    int64_t n[3] = {0, 0, 0};
+    int tmax[3] = {0, 0, 0};
+};
+// Fills list[] (host, room for npix entries) and plan.n / plan.tmax from the
+// segment offsets off[0..npix] (host); plan.pix is left for the caller to set
+// to a device copy of list.
+void attention_plan(const int64_t *off, int64_t npix, int32_t *list, AttnPlan &plan);
+void launch_attention_plan(const __nv_bfloat16 *qkv, Segs segs, const AttnPlan &plan, int64_t ntok,
+                           __nv_bfloat16 *att, int *status, cudaStream_t st);
+// Every pixel with the same series length Tmax (segs describes uniform or
+// offset segments): one class, one launch.
 void launch_attention(const __nv_bfloat16 *qkv, Segs segs, int64_t npix, int64_t ntok, int Tmax, __nv_bfloat16 *att,
                       int *status, cudaStream_t st);
 
