@@ -1187,8 +1187,9 @@ static bool attention_pipelined() {
     return on;
 }
 
-// TC_ATTN_TC: 0 = always the mma.sync kernel, 1 (default) = the cheaper of the
-// two by the cost model below, 2 = the tcgen05 kernel whenever T <= 128.
+// TC_ATTN_TC: 0 = always the mma.sync kernel, 1 (default) = the tcgen05 kernel
+// for a series longer than AT_MMA_MAX_T and up to 128 steps, 2 = the tcgen05
+// kernel whenever T <= 128.
 static int attention_tcgen05() {
     static const int mode = [] {
         const char *e = std::getenv("TC_ATTN_TC");

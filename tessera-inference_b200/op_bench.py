@@ -9,9 +9,9 @@ launch and the bandwidth they give. Attention bytes per token are the Q, K and
 V rows read (3 x 640 bf16) and the output row written (640 bf16): 5,120 B.
 LayerNorm bytes per row are 640 bf16 read and written: 2,560 B. Inputs are
 seeded random bf16 in device memory, larger than L2 at the default sizes.
-`TC_ATTN_TC=2` selects the tcgen05 attention kernel for every chunk of series
-up to 128 steps and `TC_ATTN_TC=0` the mma.sync kernel; unset, the library
-chooses per chunk.
+`TC_ATTN_TC=2` selects the tcgen05 attention kernel for every series of up
+to 128 steps and `TC_ATTN_TC=0` the mma.sync kernel; unset, the library
+takes tcgen05 for series longer than 48 steps and up to 128.
 
 The chunk is described by its series length alone (no offsets array), so the
 entry point does no host work and the launches run back to back.
