@@ -82,6 +82,17 @@ int tcb_op_ln_relu2560(void *r, int64_t P, const float *g, const float *b, void 
 int tcb_op_out128(const void *r2, int64_t P, const uint8_t *empty, float *out, int8_t *codes, float *scales,
                   void *stream);
 
+/* Attention kernel classes of a chunk's pixels (host only, no CUDA call; no
+ * reference counterpart: the reference has one attention path). off[0..npix]
+ * are the segment offsets. list receives the pixels with a non-empty series,
+ * class by class in pixel order: class 0 the mma.sync kernel for T <= 48,
+ * class 1 the tcgen05 kernel for 48 < T <= 128, class 2 the mma.sync kernel
+ * for T > 128 (TC_ATTN_TC=0 / 2 move every T <= 128 to class 0 / 1).
+ * n[3] receives the pixels per class and tmax[3] the longest series per
+ * class. The class of a pixel depends on its own length only. Returns 0, or
+ * -1 on bad arguments (null pointers, negative npix, decreasing offsets). */
+int tcb_attention_plan(const int64_t *off, int64_t npix, int32_t *list, int64_t *n, int32_t *tmax);
+
 /* Failure-detection probe (no reference counterpart: the reference has no
  * device-side waits). One kernel waits limit_us on an mbarrier that nothing
  * signals, through the same bounded wait every pipeline kernel uses, then

@@ -1057,6 +1057,25 @@ int tcb_op_out128(const void *r2, int64_t P, const uint8_t *empty, float *out, i
                                           static_cast<cudaStream_t>(stream)))
 }
 
+int tcb_attention_plan(const int64_t *off, int64_t npix, int32_t *list, int64_t *n, int32_t *tmax) {
+    // host arithmetic only: no CUDA call, so it runs without a GPU
+    try {
+        if (!off || !list || !n || !tmax || npix < 0) throw std::runtime_error("bad arguments");
+        for (int64_t i = 0; i < npix; ++i)
+            if (off[i + 1] < off[i]) throw std::runtime_error("decreasing offsets");
+        AttnPlan plan;
+        attention_plan(off, npix, list, plan);
+        for (int c = 0; c < 3; ++c) {
+            n[c] = plan.n[c];
+            tmax[c] = plan.tmax[c];
+        }
+        return 0;
+    } catch (const std::exception &e) {
+        std::fprintf(stderr, "tcb_attention_plan: %s\n", e.what());
+        return -1;
+    }
+}
+
 int tcb_op_wait_probe(int64_t limit_us, int *status, void *stream) {
     OP_TRY("tcb_op_wait_probe", launch_wait_probe((uint64_t)std::max<int64_t>(limit_us, 0) * 1000, status,
                                                   static_cast<cudaStream_t>(stream)))

@@ -23,7 +23,7 @@ EXPORTED = [
     "tc_plan_rows", "tc_set_stream", "tc_set_profiling", "tc_get_stats", "tc_reset_stats", "tc_host_alloc",
     "tc_host_free",
     "tcb_op_gemm", "tcb_op_gemm_ln", "tcb_op_gemm_ln_noalloc", "tcb_op_count", "tcb_op_gather", "tcb_op_emb1", "tcb_op_attention",
-    "tcb_op_layernorm640", "tcb_op_pool", "tcb_op_ln_relu2560", "tcb_op_out128", "tcb_op_wait_probe",
+    "tcb_op_layernorm640", "tcb_op_pool", "tcb_op_ln_relu2560", "tcb_op_out128", "tcb_op_wait_probe", "tcb_attention_plan",
 ]
 
 CAT_NAMES = ["h2d", "prep", "emb1", "gemm", "attention", "layernorm", "pool", "head", "d2h"]
@@ -113,6 +113,8 @@ def load_library(path: os.PathLike | None = None) -> C.CDLL:
     lib.tcb_op_ln_relu2560.argtypes = [vp, i64, vp, vp, vp]
     lib.tcb_op_wait_probe.restype = i32
     lib.tcb_op_wait_probe.argtypes = [i64, vp, vp]
+    lib.tcb_attention_plan.restype = i32
+    lib.tcb_attention_plan.argtypes = [vp, i64, vp, vp, vp]
     lib.tcb_op_out128.restype = i32
     lib.tcb_op_out128.argtypes = [vp, i64, vp, vp, vp, vp, vp]
     if path is None:
@@ -211,6 +213,21 @@ class Encoder:
 
     def profile_dump(self):
         self.lib.tc_profile_dump(self.h)
+
+
+def attention_plan(off: np.ndarray) -> tuple[list[np.ndarray], list[int]]:
+    """tcb_attention_plan: the pixels of each attention class (0: mma.sync,
+    1: tcgen05, 2: mma.sync for T > 128) and each class's longest series."""
+    lib = load_library()
+    off = np.ascontiguousarray(off, dtype=np.int64)
+    npix = len(off) - 1
+    lst = np.zeros(max(npix, 1), np.int32)
+    n = np.zeros(3, np.int64)
+    tmax = np.zeros(3, np.int32)
+    if lib.tcb_attention_plan(_ptr(off), npix, _ptr(lst), _ptr(n), _ptr(tmax)) != 0:
+        raise RuntimeError("tcb_attention_plan failed")
+    b = np.concatenate([[0], np.cumsum(n)])
+    return [lst[b[c]:b[c + 1]].copy() for c in range(3)], [int(t) for t in tmax]
 
 
 def plan_rows(tile: dict, nparts: int) -> list[int]:

@@ -142,3 +142,32 @@ def test_host_alloc_rejects_nonpositive():
     assert lib.tc_host_alloc(0) is None
     assert lib.tc_host_alloc(-5) is None
     lib.tc_host_free(None)
+
+
+def test_attention_classes_follow_each_pixel_alone():
+    """Every pixel's attention kernel follows its own series length (bins of
+    the reference driver: 1 for an empty modality, multiples of 8 up to 256,
+    0 for a pixel with no token), so a pixel's result cannot depend on the
+    chunk, row band or device it shares with other pixels."""
+    rng = np.random.default_rng(5)
+    lens = rng.choice([0, 1, 8, 40, 48, 56, 64, 120, 128, 136, 200, 256], size=500)
+    off = np.concatenate([[0], np.cumsum(lens)])
+    classes, tmax = tb.attention_plan(off)
+    want = [np.flatnonzero((lens > 0) & (lens <= 48)), np.flatnonzero((lens > 48) & (lens <= 128)),
+            np.flatnonzero(lens > 128)]
+    for c in range(3):
+        np.testing.assert_array_equal(classes[c], want[c])
+        assert tmax[c] == (int(lens[want[c]].max()) if len(want[c]) else 0)
+    # any sub-range (a chunk or row band) puts each pixel in the same class
+    for a, b in ((0, 37), (37, 38), (100, 499)):
+        sub, _ = tb.attention_plan(off[a:b + 1] - off[a])
+        for c in range(3):
+            np.testing.assert_array_equal(sub[c] + a, want[c][(want[c] >= a) & (want[c] < b)])
+    empty, t0 = tb.attention_plan(np.zeros(1, np.int64))
+    assert all(len(x) == 0 for x in empty) and t0 == [0, 0, 0]
+    lib = tb.load_library()
+    bad = np.array([0, 5, 3], np.int64)
+    out = np.zeros(4, np.int64)
+    assert lib.tcb_attention_plan(tb._ptr(bad), 2, tb._ptr(np.zeros(2, np.int32)), tb._ptr(out),
+                                  tb._ptr(np.zeros(3, np.int32))) == -1
+
