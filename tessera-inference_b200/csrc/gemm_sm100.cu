@@ -102,6 +102,50 @@ __device__ __forceinline__ void epilogue_cols16(const GemmArgs &p, const uint32_
                       pack_bf16x2(v[14], v[15]));
 }
 
+// Lane `src`'s pointer, for every lane of the warp.
+__device__ __forceinline__ const bf16 *shfl_ptr(const bf16 *ptr, int src) {
+    const unsigned long long v = reinterpret_cast<unsigned long long>(ptr);
+    return reinterpret_cast<const bf16 *>(__shfl_sync(0xFFFFFFFFu, v, src));
+}
+
+// The residual of a 32-column group (two = true) or a 16-column one, in the
+// coalesced pattern: 32 columns are rows i * 8 + lane / 4 (i < 4, pointers
+// r0..r3), 16 bytes at lane % 4; 16 columns are rows i * 16 + lane / 2 (i < 2),
+// 16 bytes at lane % 2. A null row pointer gives zeros.
+__device__ __forceinline__ void res_load_group(const bf16 *res_row, const bf16 *r0, const bf16 *r1,
+                                               const bf16 *r2, const bf16 *r3, int n0, int c, bool two, int lane,
+                                               uint4 &g0, uint4 &g1, uint4 &g2, uint4 &g3) {
+    const uint4 zero = make_uint4(0, 0, 0, 0);
+    if (two) {
+        const int k = lane & 3;
+        g0 = r0 ? reinterpret_cast<const uint4 *>(r0 + n0 + c)[k] : zero;
+        g1 = r1 ? reinterpret_cast<const uint4 *>(r1 + n0 + c)[k] : zero;
+        g2 = r2 ? reinterpret_cast<const uint4 *>(r2 + n0 + c)[k] : zero;
+        g3 = r3 ? reinterpret_cast<const uint4 *>(r3 + n0 + c)[k] : zero;
+    } else {
+        const int k = lane & 1;
+        const bf16 *h0 = shfl_ptr(res_row, lane >> 1), *h1 = shfl_ptr(res_row, 16 + (lane >> 1));
+        g0 = h0 ? reinterpret_cast<const uint4 *>(h0 + n0 + c)[k] : zero;
+        g1 = h1 ? reinterpret_cast<const uint4 *>(h1 + n0 + c)[k] : zero;
+    }
+}
+// Write a group loaded by res_load_group into the staging rows (same swizzle
+// as the output staging: chunk k of row rr at position k ^ ((rr >> 1) & 3)).
+__device__ __forceinline__ void res_stage_group(uint8_t *stage, bool two, int lane, const uint4 &g0, const uint4 &g1,
+                                                const uint4 &g2, const uint4 &g3) {
+    if (two) {
+        const int k = lane & 3, r = lane >> 2;
+        reinterpret_cast<uint4 *>(stage + r * 64)[k ^ ((r >> 1) & 3)] = g0;
+        reinterpret_cast<uint4 *>(stage + (r + 8) * 64)[k ^ (((r + 8) >> 1) & 3)] = g1;
+        reinterpret_cast<uint4 *>(stage + (r + 16) * 64)[k ^ (((r + 16) >> 1) & 3)] = g2;
+        reinterpret_cast<uint4 *>(stage + (r + 24) * 64)[k ^ (((r + 24) >> 1) & 3)] = g3;
+    } else {
+        const int k = lane & 1, r = lane >> 1;
+        reinterpret_cast<uint4 *>(stage + r * 64)[k ^ ((r >> 1) & 3)] = g0;
+        reinterpret_cast<uint4 *>(stage + (r + 16) * 64)[k ^ (((r + 16) >> 1) & 3)] = g1;
+    }
+}
+
 // One epilogue warp: output rows row_base .. row_base + 31 (its TMEM lane
 // quadrant, one row per lane) and accumulator columns [c0, c1) of a tile whose
 // first output column is n0. Per group of 32 columns: TMEM -> registers ->
@@ -109,8 +153,11 @@ __device__ __forceinline__ void epilogue_cols16(const GemmArgs &p, const uint32_
 // swizzled so both the row-wise writes and the read-back are conflict-free) ->
 // row-contiguous 64-byte global stores, 8 rows per instruction.
 // The residual (or, for an integer day of year, the DOY-table row, which is
-// an ordinary residual row) is software-pipelined one group ahead, and the
-// first group's loads are issued before waiting for the accumulator.
+// an ordinary residual row) takes the same way in reverse: loaded 8 rows x 64
+// contiguous bytes per instruction (the row pointers passed between lanes by
+// shuffle), written into the staging buffer and read back one row per lane.
+// Its loads run one group ahead, the first group's before the wait for the
+// accumulator.
 // Returns false if the wait for the accumulator gave up.
 __device__ __forceinline__ bool epilogue_tile(const GemmArgs &p, uint32_t tbase, int row_base, int n0, int c0, int c1,
                                               uint8_t *stage, int lane, uint64_t *tfull_bar, uint32_t parity,
@@ -129,25 +176,40 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs &p, uint32_t tbase,
             else pe_irregular = true;
         }
     }
-    uint4 qn[4] = {};
-    auto load_group = [&](int c, uint4 (&q)[4]) {
-        if (res_row) {
-            const uint4 *r4 = reinterpret_cast<const uint4 *>(res_row + n0 + c);
-            q[0] = r4[0];
-            q[1] = r4[1];
-            if (c + 32 <= c1) { q[2] = r4[2]; q[3] = r4[3]; }
-        }
-    };
-    load_group(c0, qn);
-    if (!mbar_wait(tfull_bar, parity, abort_flag, p.status, ERR_WAIT_TMEM_FULL)) return false;
-    tc_fence_after();
+    const bool any_res = p.res != nullptr || p.pe_doy != nullptr;  // uniform
+    // residual rows of the coalesced pattern: row i * 8 + lane / 4, 16 bytes at lane % 4
+    const bf16 *rp0 = nullptr, *rp1 = nullptr, *rp2 = nullptr, *rp3 = nullptr;
+    if (any_res) {
+        rp0 = shfl_ptr(res_row, (lane >> 2));
+        rp1 = shfl_ptr(res_row, 8 + (lane >> 2));
+        rp2 = shfl_ptr(res_row, 16 + (lane >> 2));
+        rp3 = shfl_ptr(res_row, 24 + (lane >> 2));
+    }
     uint4 *my_row = reinterpret_cast<uint4 *>(stage + lane * 64);
     const int sw = (lane >> 1) & 3;
+    uint4 g0 = make_uint4(0, 0, 0, 0), g1 = g0, g2 = g0, g3 = g0;
+    if (any_res) res_load_group(res_row, rp0, rp1, rp2, rp3, n0, c0, c0 + 32 <= c1, lane, g0, g1, g2, g3);
+    if (!mbar_wait(tfull_bar, parity, abort_flag, p.status, ERR_WAIT_TMEM_FULL)) return false;
+    tc_fence_after();
 #pragma unroll 1
     for (int c = c0; c < c1; c += 32) {
         const bool two = c + 32 <= c1;
-        const uint4 q0[2] = {qn[0], qn[1]}, q1[2] = {qn[2], qn[3]};
-        if (c + 32 < c1) load_group(c + 32, qn);
+        uint4 q[4] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
+        if (any_res) {
+            // the group's residual, from the coalesced layout to one row per lane
+            res_stage_group(stage, two, lane, g0, g1, g2, g3);
+            __syncwarp();
+            q[0] = my_row[0 ^ sw];
+            q[1] = my_row[1 ^ sw];
+            if (two) {
+                q[2] = my_row[2 ^ sw];
+                q[3] = my_row[3 ^ sw];
+            }
+            __syncwarp();
+            if (c + 32 < c1)
+                res_load_group(res_row, rp0, rp1, rp2, rp3, n0, c + 32, c + 64 <= c1, lane, g0, g1, g2, g3);
+        }
+        const uint4 q0[2] = {q[0], q[1]}, q1[2] = {q[2], q[3]};
         uint32_t r0[16], r1[16];
         tmem_ld16(tbase + (uint32_t)c, r0);
         if (two) tmem_ld16(tbase + (uint32_t)(c + 16), r1);
