@@ -63,7 +63,12 @@ int tcb_op_gather(int modality, const uint16_t *bands, const uint8_t *masks, con
 int tcb_op_emb1(int C, const float *rec, int64_t M, const float *w1t, const float *b1, void *y, void *stream);
 
 /* Self-attention per pixel segment (src/tessera_cpu.cpp:333-352,410-418).
- * off (npix+1 entries) or, when NULL, uniform segments of uniform_T tokens. */
+ * off (npix+1 entries, device memory) or, when NULL, uniform segments of
+ * uniform_T tokens. Each pixel's kernel follows its own length, as in the
+ * tile path (tcb_attention_plan): with offsets the call reads them back,
+ * lists the pixels by class, runs one launch per class and synchronizes the
+ * stream before returning. Tmax must be at least every segment's length
+ * (-1 otherwise) and at most 256. */
 int tcb_op_attention(const void *qkv, const int64_t *off, int64_t uniform_T, int64_t npix, int Tmax, void *att,
                      void *stream);
 
