@@ -171,3 +171,26 @@ def test_attention_classes_follow_each_pixel_alone():
     assert lib.tcb_attention_plan(tb._ptr(bad), 2, tb._ptr(np.zeros(2, np.int32)), tb._ptr(out),
                                   tb._ptr(np.zeros(3, np.int32))) == -1
 
+
+
+@pytest.mark.parametrize("mode,want_small,want_tc", [("0", lambda t: t <= 128, lambda t: False),
+                                                     ("2", lambda t: False, lambda t: t <= 128)])
+def test_attention_classes_forced_modes(mode, want_small, want_tc):
+    """TC_ATTN_TC=0 sends every series of up to 128 steps to mma.sync, =2 to
+    tcgen05; longer series always stay on mma.sync (the mode is read once per
+    process, so each runs in its own)."""
+    import json
+    import os
+    import subprocess
+    import sys
+    code = ("import sys, json, numpy as np; sys.path[:0] = [sys.argv[1]]; import tessera_b200 as tb; "
+            "lens = np.array([1, 8, 48, 56, 128, 136, 256, 0]); off = np.concatenate([[0], np.cumsum(lens)]); "
+            "c, t = tb.attention_plan(off); print(json.dumps([x.tolist() for x in c]))")
+    env = dict(os.environ, TC_ATTN_TC=mode)
+    r = subprocess.run([sys.executable, "-c", code, str(REPO / "tessera-inference_b200")], capture_output=True,
+                       text=True, env=env, check=True)
+    classes = json.loads(r.stdout.strip().splitlines()[-1])
+    lens = [1, 8, 48, 56, 128, 136, 256, 0]
+    assert classes[0] == [i for i, t in enumerate(lens) if t > 0 and want_small(t)]
+    assert classes[1] == [i for i, t in enumerate(lens) if t > 0 and want_tc(t)]
+    assert classes[2] == [i for i, t in enumerate(lens) if t > 128]
