@@ -392,13 +392,12 @@ static void backbone(Dev &d, int b, const float *rec, Segs segs, int64_t M, int 
         for (int l = 0; l < NL; ++l) {
             gemm(d, GK_QKV, B.qkv[l], d.x.p, M, d.qkv.p, false);
             d.mark(TC_CAT_ATTN);
-            if (plan) launch_attention_plan(d.qkv.p, segs, *plan, M, d.att.p, d.status.p, d.st);
-            else launch_attention(d.qkv.p, segs, npix, M, Tmax, d.att.p, d.status.p, d.st);
+            d.stats.launches += plan ? launch_attention_plan(d.qkv.p, segs, *plan, M, d.att.p, d.status.p, d.st)
+                                     : launch_attention(d.qkv.p, segs, npix, M, Tmax, d.att.p, d.status.p, d.st);
             if (ln_fused()) {  // LN1 / LN2 in the epilogues of out-proj / FFN2
                 gemm(d, GK_OUT, B.out[l], d.att.p, M, d.x1.p, false, d.x.p, nullptr, 1, B.ln1g[l], B.ln1b[l]);
                 gemm(d, GK_FFN1, B.ffn1[l], d.x1.p, M, d.hbuf.p, true);
                 gemm(d, GK_FFN2, B.ffn2[l], d.hbuf.p, M, d.x.p, false, d.x1.p, nullptr, 1, B.ln2g[l], B.ln2b[l]);
-                d.stats.launches += 1;
             } else {
                 gemm(d, GK_OUT, B.out[l], d.att.p, M, d.y.p, false, d.x.p);
                 d.mark(TC_CAT_LN);
@@ -407,7 +406,7 @@ static void backbone(Dev &d, int b, const float *rec, Segs segs, int64_t M, int 
                 gemm(d, GK_FFN2, B.ffn2[l], d.hbuf.p, M, d.y.p, false, d.x1.p);
                 d.mark(TC_CAT_LN);
                 launch_layernorm640(d.y.p, M, B.ln2g[l], B.ln2b[l], d.x.p, d.st);
-                d.stats.launches += 3;
+                d.stats.launches += 2;
             }
         }
     }

@@ -1274,23 +1274,29 @@ static void attention_of_class(int cls, const bf16 *qkv, Segs segs, int64_t npix
     }
 }
 
-void launch_attention_plan(const bf16 *qkv, Segs segs, const AttnPlan &plan, int64_t ntok, bf16 *att, int *status,
-                           cudaStream_t st) {
+int launch_attention_plan(const bf16 *qkv, Segs segs, const AttnPlan &plan, int64_t ntok, bf16 *att, int *status,
+                          cudaStream_t st) {
     int64_t o = 0;
+    int launched = 0;
     for (int c = 0; c < 3; ++c) {
         Segs s = segs;
         s.pix = plan.pix + o;
-        attention_of_class(c, qkv, s, plan.n[c], ntok, plan.tmax[c], att, status, st);
+        if (plan.n[c] > 0 && plan.tmax[c] > 0) {
+            attention_of_class(c, qkv, s, plan.n[c], ntok, plan.tmax[c], att, status, st);
+            ++launched;
+        }
         o += plan.n[c];
     }
     check_launch("k_attention");
+    return launched;
 }
 
-void launch_attention(const bf16 *qkv, Segs segs, int64_t npix, int64_t ntok, int Tmax, bf16 *att, int *status,
-                      cudaStream_t st) {
-    if (npix <= 0 || Tmax <= 0) return;
+int launch_attention(const bf16 *qkv, Segs segs, int64_t npix, int64_t ntok, int Tmax, bf16 *att, int *status,
+                     cudaStream_t st) {
+    if (npix <= 0 || Tmax <= 0) return 0;
     attention_of_class(attention_class(Tmax), qkv, segs, npix, ntok, Tmax, att, status, st);
     check_launch("k_attention");
+    return 1;
 }
 
 void launch_layernorm640(const bf16 *x, int64_t M, const float *g, const float *b, bf16 *y, cudaStream_t st) {

@@ -71,12 +71,13 @@ struct AttnPlan {
 // segment offsets off[0..npix] (host); plan.pix is left for the caller to set
 // to a device copy of list.
 void attention_plan(const int64_t *off, int64_t npix, int32_t *list, AttnPlan &plan);
-void launch_attention_plan(const __nv_bfloat16 *qkv, Segs segs, const AttnPlan &plan, int64_t ntok,
-                           __nv_bfloat16 *att, int *status, cudaStream_t st);
+// Both return the number of kernels launched (one per non-empty class).
+int launch_attention_plan(const __nv_bfloat16 *qkv, Segs segs, const AttnPlan &plan, int64_t ntok,
+                          __nv_bfloat16 *att, int *status, cudaStream_t st);
 // Every pixel with the same series length Tmax (segs describes uniform or
 // offset segments): one class, one launch.
-void launch_attention(const __nv_bfloat16 *qkv, Segs segs, int64_t npix, int64_t ntok, int Tmax, __nv_bfloat16 *att,
-                      int *status, cudaStream_t st);
+int launch_attention(const __nv_bfloat16 *qkv, Segs segs, int64_t npix, int64_t ntok, int Tmax, __nv_bfloat16 *att,
+                     int *status, cudaStream_t st);
 
 // y = bf16(LN(x) * g + b) over rows of 640 (g, b may be null for no affine).
 void launch_layernorm640(const __nv_bfloat16 *x, int64_t M, const float *g, const float *b, __nv_bfloat16 *y,
