@@ -27,7 +27,6 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
-#include <fstream>
 #include <mutex>
 #include <sstream>
 #include <stdexcept>
@@ -35,6 +34,7 @@
 #include <thread>
 #include <vector>
 
+#include "npy.h"
 #include "tessera_b200.h"
 
 namespace {
@@ -67,66 +67,18 @@ struct Array {
     }
 };
 
-// .npy version 1/2/3 reader: C-order arrays of the expected dtype, payload read
-// straight into the array's page-locked buffer.
-void read_npy(const std::string &path, const char *want_descr, Array &a) {
-    std::ifstream f(path, std::ios::binary);
-    if (!f) throw std::runtime_error("cannot open " + path);
-    char magic[6];
-    f.read(magic, 6);
-    if (!f || std::memcmp(magic, "\x93NUMPY", 6)) throw std::runtime_error("not a .npy file: " + path);
-    unsigned char ver[2];
-    f.read(reinterpret_cast<char *>(ver), 2);
-    uint32_t hlen = 0;
-    if (ver[0] == 1) {
-        uint16_t h = 0;
-        f.read(reinterpret_cast<char *>(&h), 2);
-        hlen = h;
-    } else {
-        f.read(reinterpret_cast<char *>(&hlen), 4);
-    }
-    if (!f || hlen > (1u << 20)) throw std::runtime_error("bad npy header length in " + path);
-    std::string hdr(hlen, '\0');
-    f.read(&hdr[0], hlen);
-    auto value_at = [&](const char *key) {
-        const size_t k = hdr.find(std::string("'") + key + "'");
-        if (k == std::string::npos) throw std::runtime_error("npy header of " + path + " has no " + key);
-        return hdr.find(':', k) + 1;
-    };
-    const size_t d0 = hdr.find('\'', value_at("descr"));
-    a.descr = hdr.substr(d0 + 1, hdr.find('\'', d0 + 1) - d0 - 1);
-    const size_t fo = value_at("fortran_order");
-    if (hdr.compare(hdr.find_first_not_of(' ', fo), 4, "True") == 0)
-        throw std::runtime_error("fortran-order npy not supported: " + path);
-    if (a.descr != want_descr)
-        throw std::runtime_error(path + ": expected dtype " + want_descr + ", got " + a.descr);
-    const size_t s0 = hdr.find('(', value_at("shape")), s1 = hdr.find(')', s0);
-    a.shape.clear();
-    std::stringstream ss(hdr.substr(s0 + 1, s1 - s0 - 1));
-    for (std::string tok; std::getline(ss, tok, ',');)
-        if (tok.find_first_not_of(' ') != std::string::npos) a.shape.push_back(std::stoll(tok));
-    const size_t bytes = (size_t)a.count() * (size_t)std::stoi(a.descr.substr(2));
-    a.buf.reserve(bytes);
-    f.read(static_cast<char *>(a.buf.p), (std::streamsize)bytes);
-    if (!f) throw std::runtime_error("truncated npy: " + path);
-}
-
-void write_npy(const std::string &path, const char *descr, const std::vector<int64_t> &shape, const void *data,
-               size_t bytes) {
-    std::string sh = "(";
-    for (size_t i = 0; i < shape.size(); ++i) sh += (i ? ", " : "") + std::to_string(shape[i]);
-    sh += shape.size() == 1 ? ",)" : ")";
-    std::string hdr = std::string("{'descr': '") + descr + "', 'fortran_order': False, 'shape': " + sh + ", }";
-    const size_t unpadded = 10 + hdr.size() + 1;  // magic + version + length, header, '\n'
-    hdr.append((64 - unpadded % 64) % 64, ' ');
-    hdr += '\n';
-    std::ofstream f(path, std::ios::binary);
-    f.write("\x93NUMPY\x01\x00", 8);
-    const uint16_t hl = (uint16_t)hdr.size();
-    f.write(reinterpret_cast<const char *>(&hl), 2);
-    f.write(hdr.data(), (std::streamsize)hdr.size());
-    f.write(static_cast<const char *>(data), (std::streamsize)bytes);
-    if (!f) throw std::runtime_error("write failed: " + path);
+// Reads one array of the tile into its page-locked buffer, checking the
+// element type the reference driver requires (src/tessera_encode.cpp:237-243).
+void load_array(const std::string &path, char kind, int size, Array &a) {
+    npy::read(path, [&](const npy::Header &h) -> void * {
+        if (!h.is(kind, size))
+            throw std::runtime_error(path + ": element type " + h.descr + ", this input must be " +
+                                     (size == 1 ? "|" : "<") + kind + std::to_string(size));
+        a.descr = h.descr;
+        a.shape = h.shape;
+        a.buf.reserve((size_t)h.nbytes());
+        return a.buf.p;
+    });
 }
 
 bool exists(const std::string &p) {
@@ -160,13 +112,13 @@ void load_tile(const std::string &dir_in, TileIn &t) {
     t.grid = d.substr(d.rfind('/') + 1);
     const bool sub = exists(d + "/s2");
     const std::string s2 = sub ? d + "/s2/" : d + "/", s1 = sub ? d + "/s1/" : d + "/";
-    read_npy(s2 + "bands.npy", "<u2", t.bands);
-    read_npy(s2 + "masks.npy", "|u1", t.masks);
-    read_npy(s2 + "doys.npy", "<u2", t.doys);
-    read_npy(s1 + "sar_ascending.npy", "<i2", t.asc);
-    read_npy(s1 + "sar_ascending_doy.npy", "<i2", t.asc_doy);
-    read_npy(s1 + "sar_descending.npy", "<i2", t.desc);
-    read_npy(s1 + "sar_descending_doy.npy", "<i2", t.desc_doy);
+    load_array(s2 + "bands.npy", 'u', 2, t.bands);
+    load_array(s2 + "masks.npy", 'u', 1, t.masks);
+    load_array(s2 + "doys.npy", 'u', 2, t.doys);
+    load_array(s1 + "sar_ascending.npy", 'i', 2, t.asc);
+    load_array(s1 + "sar_ascending_doy.npy", 'i', 2, t.asc_doy);
+    load_array(s1 + "sar_descending.npy", 'i', 2, t.desc);
+    load_array(s1 + "sar_descending_doy.npy", 'i', 2, t.desc_doy);
     if (t.bands.shape.size() != 4 || t.bands.shape[3] != 10) throw std::runtime_error(t.grid + ": bands must be (T2,H,W,10)");
     t.T2 = t.bands.shape[0];
     t.H = t.bands.shape[1];
@@ -283,10 +235,10 @@ int main(int argc, char **argv) {
             if (o.err.empty()) {
                 try {
                     const auto t0 = clk::now();
-                    write_npy(out_dir + "/" + o.grid + ".npy", "|i1", {o.H, o.W, 128}, o.codes.p,
-                              (size_t)(o.H * o.W * 128));
-                    write_npy(out_dir + "/" + o.grid + "_scales.npy", "<f4", {o.H, o.W}, o.scales.p,
-                              (size_t)(o.H * o.W) * 4);
+                    npy::write(out_dir + "/" + o.grid + ".npy", "|i1", {o.H, o.W, 128}, o.codes.p,
+                               (uint64_t)(o.H * o.W * 128));
+                    npy::write(out_dir + "/" + o.grid + "_scales.npy", "<f4", {o.H, o.W}, o.scales.p,
+                               (uint64_t)(o.H * o.W) * 4);
                     o.write_s = since(t0);
                     std::printf("ENCODE grid=%s px=%ld devices=%d  load=%.2fs net=%.2fs write=%.2fs\n", o.grid.c_str(),
                                 (long)(o.H * o.W), ndev, o.load_s, o.net_s, o.write_s);

@@ -14,6 +14,10 @@
       export_ref.json: for synth.fake_checkpoint in f32 and in bf16, the
       sha256 and size of the .tcw that the reference's unmodified
       tools/export_weights.py writes (run here, from the reference tree).
+  python tests/golden/make_golden.py api
+      ref_api.json: the tokens of the four back-end prototypes
+      (tc_create / tc_encode / tc_profile_dump / tc_destroy) as the reference
+      driver declares them (src/tessera_encode.cpp:47-52).
   python tests/golden/make_golden.py refcuda       (on a B200)
       Runs the reference's unmodified driver + CUDA back end
       (oracle/_ref/tessera_encode_cuda_ref, built by `make -C oracle cuda-ref`)
@@ -156,9 +160,43 @@ def refcuda():
             print(name, codes.shape)
 
 
+API_NAMES = ("tc_create", "tc_encode", "tc_profile_dump", "tc_destroy")
+
+
+def c_prototypes(text: str, names=API_NAMES) -> dict:
+    """name -> token list of its declaration `ret name(params);` in C source
+    text (comments removed, whitespace ignored)."""
+    import re
+    text = re.sub(r"/\*.*?\*/", " ", text, flags=re.S)
+    text = re.sub(r"//[^\n]*", " ", text)
+    out = {}
+    for n in names:
+        m = re.search(r"(?:^|[;{}])\s*([A-Za-z_][\w\s\*]*?\b" + n + r"\s*\([^)]*\)\s*;)", text, flags=re.M)
+        if m:
+            out[n] = re.findall(r"\w+|[^\s\w]", m.group(1))
+    return out
+
+
+def reference_root() -> Path:
+    return Path(os.environ.get("REFERENCE_ROOT", "/root/reference"))
+
+
+def api():
+    """ref_api.json: the token lists of the four back-end prototypes the
+    reference driver declares (src/tessera_encode.cpp:47-52)."""
+    src = reference_root() / "src" / "tessera_encode.cpp"
+    if not src.exists():
+        sys.exit(f"the reference driver is needed: {src}")
+    protos = c_prototypes(src.read_text())
+    if set(protos) != set(API_NAMES):
+        sys.exit(f"could not find all four prototypes in {src}: {sorted(protos)}")
+    (HERE / "ref_api.json").write_text(json.dumps(protos, indent=1) + "\n")
+    print({k: " ".join(v) for k, v in protos.items()})
+
+
 def export():
     import torch
-    script = Path(os.environ.get("REFERENCE_ROOT", "/root/reference")) / "tools" / "export_weights.py"
+    script = reference_root() / "tools" / "export_weights.py"
     if not script.exists():
         sys.exit(f"the reference's exporter is needed: {script}")
     res = {}
@@ -182,5 +220,7 @@ if __name__ == "__main__":
         driver()
     if cmd in ("export", "all"):
         export()
+    if cmd in ("api", "all"):
+        api()
     if cmd == "refcuda":
         refcuda()

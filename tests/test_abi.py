@@ -30,6 +30,26 @@ def test_headers_declare_reference_api():
     assert len(names) >= 20
 
 
+def test_reference_prototypes_token_for_token():
+    """The four back-end prototypes of include/tessera_b200.h are the ones the
+    reference driver declares (src/tessera_encode.cpp:47-52), token for token:
+    return type, name, parameter types and names. The reference's tokens are
+    the committed fixture tests/golden/ref_api.json (make_golden.py api); when
+    the reference tree is on this machine it is read directly as well."""
+    import json
+    import os
+    from pathlib import Path
+    from golden.make_golden import API_NAMES, c_prototypes
+    ours = c_prototypes((REPO / "include" / "tessera_b200.h").read_text())
+    want = json.loads((REPO / "tests" / "golden" / "ref_api.json").read_text())
+    assert set(want) == set(API_NAMES)
+    for n in API_NAMES:
+        assert ours.get(n) == want[n], (n, ours.get(n), want[n])
+    src = Path(os.environ.get("REFERENCE_ROOT", "/root/reference")) / "src" / "tessera_encode.cpp"
+    if src.exists():
+        assert c_prototypes(src.read_text()) == ours
+
+
 def test_library_exports_every_declared_symbol():
     lib = tb.load_library()
     missing = [n for n in declared_functions() if not hasattr(lib, n)]

@@ -68,4 +68,4 @@ def test_driver_rejects_wrong_dtype(tmp_path):
     np.save(d / "s2" / "masks.npy", t["masks"].astype(np.int16))
     r = run_driver([d], tmp_path / "out", case_weights("cfg0", tmp_path))
     assert r.returncode == 1
-    assert "expected dtype |u1" in r.stderr
+    assert "masks.npy: element type <i2, this input must be |u1" in r.stderr
