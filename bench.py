@@ -147,27 +147,59 @@ def tile_bytes(t: dict) -> int:
 
 
 # ------------------------------------------------------------------ CPU reference arm
-def run_ref_driver(binary: Path, tile: dict, pixels: np.ndarray, weights: Path, work: Path, threads: int):
-    """Runs a reference driver binary on a 1 x K sub-tile; returns (wall s, ENCODE line)."""
+# The reference driver's own timing line (src/tessera_encode.cpp:366-370).
+ENCODE_RE = re.compile(r"load=([\d.]+)s bin=([\d.]+)s prep=([\d.]+)s net=([\d.]+)s quant\+write=([\d.]+)s "
+                       r"total=([\d.]+)s")
+
+
+def run_ref_driver(binary: Path, tile: dict, pixels: np.ndarray, weights: Path, work: Path, threads: int) -> dict:
+    """Runs a reference driver binary on the given flat pixels of the tile,
+    gathered into a 1 x K tile (exact: each pixel's result depends only on its
+    own series). Returns the process wall time and the driver's own ENCODE
+    timings: net = tc_encode calls only, total = the whole driver run (tile
+    load, binning, prep, network, quantisation, .npy write)."""
     sub = synth.subset_tile(tile, pixels)
     tdir = synth.write_tile_dir(sub, work / "grid_sample")
+    # TC_BLOCK / TC_BLOCK_S2 are the reference's block sizes (pixels per OpenMP
+    # task, tessera_cpu.cpp:486-489); one pixel per task keeps every core busy
+    # on a sample of a few thousand pixels, whose per-key batches are small.
     env = dict(os.environ, OMP_NUM_THREADS=str(threads), OMP_PROC_BIND="close", OMP_WAIT_POLICY="ACTIVE",
-               TC_BLOCK="4", TC_BLOCK_S2="8", TC_BATCH="4096")
+               TC_BLOCK="1", TC_BLOCK_S2="1", TC_BATCH="4096")
     t0 = time.perf_counter()
     r = subprocess.run([str(binary), str(tdir), str(work / "out"), str(weights)], env=env, capture_output=True,
                        text=True, check=True)
     wall = time.perf_counter() - t0
     line = next((l for l in r.stdout.splitlines() if l.startswith("ENCODE")), "")
-    return wall, line
+    m = ENCODE_RE.search(line)
+    if not m:
+        raise RuntimeError(f"no ENCODE timing line from {binary.name}: {r.stdout[-500:]}")
+    load, bin_, prep, net, quant, total = (float(x) for x in m.groups())
+    return {"px": int(len(pixels)), "wall_s": wall, "net_s": net, "total_s": total, "prep_s": prep,
+            "load_s": load, "quant_write_s": quant, "line": line}
 
 
-def cpu_sample_px(binary, tile, weights, work, threads, target_s: float) -> tuple[int, float]:
-    """Calibrate a sample size (pixels) that takes about target_s on this host."""
-    N = tile["masks"].shape[1] * tile["masks"].shape[2]
-    wall, _ = run_ref_driver(binary, tile, np.arange(32), weights, work, threads)
-    rate = 32 / max(wall, 1e-3)
-    k = int(min(max(rate * target_s, 32), 20000, N))
-    return k, rate
+def band_pixels(tile: dict, r0: int, nrows: int) -> np.ndarray:
+    """Flat indices of the contiguous row band [r0, r0 + nrows)."""
+    W = tile["masks"].shape[2]
+    return np.arange(r0 * W, (r0 + nrows) * W, dtype=np.int64)
+
+
+def cpu_band_rows(binary, tile, weights, work, threads, target_s: float) -> tuple[int, float]:
+    """Rows per band so that one run's network time is about target_s: a
+    64-pixel calibration run's network-only rate (its process start and weight
+    load are outside `net`)."""
+    T2, H, W = tile["masks"].shape
+    r = run_ref_driver(binary, tile, band_pixels(tile, H // 2, 1)[:64], weights, work, threads)
+    rate = 64 / max(r["net_s"], 0.05)
+    rows = int(min(max(round(target_s * rate / W), 1), H))
+    return rows, rate
+
+
+def cpu_summary(runs: list) -> dict:
+    px = sum(r["px"] for r in runs)
+    net, total, wall = (sum(r[k] for r in runs) for k in ("net_s", "total_s", "wall_s"))
+    return {"px": px, "net_px_s": px / net, "total_px_s": px / total, "wall_px_s": px / wall,
+            "fixed_cost_frac": (wall - net) / wall}
 
 
 def cpu_reference_arm(args, tile, weights, work) -> dict:
@@ -175,28 +207,50 @@ def cpu_reference_arm(args, tile, weights, work) -> dict:
     if not binary.exists():
         return {"impl": "reference", "unavailable": f"{binary.relative_to(REPO)} not built (make -C oracle)"}
     threads = os.cpu_count() or 1
-    k, _ = cpu_sample_px(binary, tile, weights, work, threads, target_s=args.cpu_step_s)
-    rng = np.random.default_rng(7)
-    N = tile["masks"].shape[1] * tile["masks"].shape[2]
-    samples = [np.sort(rng.choice(N, size=k, replace=False)) for _ in range(args.warmup + args.steps)]
+    T2, H, W = tile["masks"].shape
+    rows, _ = cpu_band_rows(binary, tile, weights, work, threads, target_s=args.cpu_step_s)
+    # each step: the next contiguous band of rows, from the middle of the tile
+    starts = [(H // 3 + i * rows) % max(H - rows + 1, 1) for i in range(args.warmup + args.steps)]
     for i in range(args.warmup):
-        run_ref_driver(binary, tile, samples[i], weights, work, threads)
-    walls = []
-    for i in range(args.steps):
-        w, line = run_ref_driver(binary, tile, samples[args.warmup + i], weights, work, threads)
-        walls.append(w)
-    pxs = k * args.steps / sum(walls)
-    sample = (f"{args.steps} steps of {k} random pixels of the config-1 tile each, run as 1x{k} tiles through the "
-              f"reference driver src/tessera_encode.cpp (unmodified; load, bin, prep, quant and write included) "
-              f"with the C++ restatement of the oneDNN CPU back end (oneDNN is not installed)")
-    cpu = {"value": pxs, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample,
-           "cpu_model": cpu_model()}
-    return {"metric": METRIC, "value": pxs, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": 1000 * statistics.mean(walls), "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "sample_px_per_step": k}, "impl": "reference",
-            "cpu_baseline": cpu, "tiles_per_hour": 3600 * pxs / 773535,
-            "e2e": {"value": pxs, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        run_ref_driver(binary, tile, band_pixels(tile, starts[i], rows), weights, work, threads)
+    runs = [run_ref_driver(binary, tile, band_pixels(tile, starts[args.warmup + i], rows), weights, work, threads)
+            for i in range(args.steps)]
+    sm = cpu_summary(runs)
+    value = sm["total_px_s"]
+    sample = (f"{args.steps} steps, each a contiguous band of {rows} rows ({rows * W} px) of the config-1 tile run "
+              f"as a 1x{rows * W} tile through the reference driver src/tessera_encode.cpp (unmodified) with the "
+              f"C++ restatement of the oneDNN CPU back end (oneDNN is not installed), TC_BLOCK=TC_BLOCK_S2=1; "
+              f"value = px / the driver's own total= time (load, bin, prep, network, quant, write); "
+              f"network-only {sm['net_px_s']:.1f} px/s; fixed cost {100 * sm['fixed_cost_frac']:.1f}% of wall")
+    cpu = {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample,
+           "cpu_model": cpu_model(), **sm}
+    return {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1000 * statistics.mean(r["total_s"] for r in runs),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic", "config": {"workload": WORKLOAD, "sample_px_per_step": rows * W,
+                                             "sample_rows_per_step": rows},
+            "impl": "reference", "cpu_baseline": cpu, "tiles_per_hour": 3600 * value / (H * W),
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def cpu_baseline_leg(tile, weights, work, target_s: float) -> dict | None:
+    """The reported CPU baseline of the B200 arm: one contiguous band of rows
+    (about target_s of network time on all host cores), network-only and
+    whole-driver rates from the driver's own timing line."""
+    binary = REPO / "oracle" / "_ref" / "tessera_encode_ref"
+    if not binary.exists():
+        return None
+    threads = os.cpu_count() or 1
+    T2, H, W = tile["masks"].shape
+    rows, _ = cpu_band_rows(binary, tile, weights, work, threads, target_s=target_s)
+    r = run_ref_driver(binary, tile, band_pixels(tile, H // 2, rows), weights, work, threads)
+    sm = cpu_summary([r])
+    return {"value": sm["total_px_s"], "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"rows {H // 2}..{H // 2 + rows - 1} ({rows * W} px, contiguous) of the config-1 tile as a "
+                      f"1x{rows * W} tile through the reference driver (unmodified) + C++ restatement of the oneDNN "
+                      f"CPU back end, TC_BLOCK=TC_BLOCK_S2=1; value = px / total= ({r['total_s']:.1f} s), "
+                      f"network-only {sm['net_px_s']:.1f} px/s ({r['net_s']:.1f} s)",
+            "cpu_model": cpu_model(), **sm}
 
 
 def cpu_model() -> str:
@@ -235,6 +289,32 @@ def refcuda_arm(args, tile, weights, work) -> dict:
             "ms_per_step": 1000 * best["total_s"], "higher_is_better": True}
 
 
+def gpu_reference_leg(tile, weights, work, chunk: int = 1024, runs: int = 3) -> dict | None:
+    """The reference's own CUDA back end (src/tessera_cuda.cu, cuBLASLt, rebuilt
+    for sm_100a) behind its own driver on the same tile and weights: one
+    warm-up run and `runs` timed runs at TC_CHUNK=chunk (its fastest setting
+    on this tile), about a minute in all. net = its tc_encode calls (H2D,
+    network, D2H), total = the whole driver run including the tile load."""
+    binary = REPO / "oracle" / "_ref" / "tessera_encode_cuda_ref"
+    if not binary.exists():
+        return None
+    tdir = synth.write_tile_dir(tile, work / "grid_cfg1")
+    env = dict(os.environ, TC_CHUNK=str(chunk), OMP_NUM_THREADS=str(os.cpu_count() or 1))
+    nets, totals = [], []
+    for i in range(1 + runs):
+        r = subprocess.run([str(binary), str(tdir), str(work / "out_refcuda"), str(weights)], env=env,
+                           capture_output=True, text=True, check=True, timeout=120)
+        m = ENCODE_RE.search(next(l for l in r.stdout.splitlines() if l.startswith("ENCODE")))
+        if i > 0:
+            nets.append(float(m.group(4)))
+            totals.append(float(m.group(6)))
+    N = tile["masks"].shape[1] * tile["masks"].shape[2]
+    return {"net_px_s": N / statistics.median(nets), "total_px_s": N / statistics.median(totals), "chunk": chunk,
+            "runs": runs, "net_s": nets, "total_s": totals,
+            "what": "reference driver + src/tessera_cuda.cu (cuBLASLt) rebuilt for sm_100a, same tile and weights; "
+                    "median of the timed runs after one warm-up"}
+
+
 # ------------------------------------------------------------------ B200 arm
 def main():
     ap = argparse.ArgumentParser()
@@ -243,8 +323,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference", "refcuda"])
     ap.add_argument("--config", type=int, default=1, choices=[0, 1, 3, 4])
-    ap.add_argument("--cpu-step-s", type=float, default=8.0, help="seconds per CPU reference sample")
+    ap.add_argument("--cpu-step-s", type=float, default=6.0, help="network seconds per CPU reference step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-gpu-reference", action="store_true", help="skip the reference CUDA back-end leg")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg (sweeps only)")
     ap.add_argument("--profile", action="store_true", help="print the per-category TCPROF table")
     args = ap.parse_args()
@@ -343,7 +424,7 @@ def main():
     barrier()
 
     # end to end: host (pinned) -> device -> host, through tc_encode_tile_rows
-    e2e_ms_max, ok = None, None
+    e2e_ms_max, e2e_ms, ok = None, None, None
     if not args.no_e2e:
         pin = {k: torch.from_numpy(np.ascontiguousarray(v)).pin_memory() for k, v in band.items()}
         pin_np = {k: v.numpy() for k, v in pin.items()}
@@ -358,11 +439,22 @@ def main():
             enc.encode_tile(pin_np, 0, R, codes_h, scales_h)
         e1.record(stream)
         torch.cuda.synchronize()
-        e2e_ms_max = max_over_ranks(e0.elapsed_time(e1))
+        e2e_ms = e0.elapsed_time(e1)
+        e2e_ms_max = max_over_ranks(e2e_ms)
         barrier()
         # the device-resident and host-buffer paths must give the same bytes
         ok = bool(np.array_equal(codes_d.cpu().numpy(), codes_h)) and bool(
             np.array_equal(scales_d.cpu().numpy().view(np.uint32), scales_h.view(np.uint32)))
+
+    # per-rank device times and row bands (under torchrun every rank takes part)
+    mine = [dev_ms, e2e_ms if e2e_ms is not None else -1.0, float(r0), float(r1)]
+    if dist is not None:
+        t = torch.tensor(mine, dtype=torch.float64, device="cuda")
+        allv = torch.zeros(world * len(mine), dtype=torch.float64, device="cuda")
+        dist.all_gather_into_tensor(allv, t)
+        per_rank = allv.view(world, len(mine)).cpu().tolist()
+    else:
+        per_rank = [mine]
 
     total_px = H * W
     value = total_px * args.steps / (dev_ms_max / 1000.0)
@@ -384,16 +476,10 @@ def main():
 
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
-        binary = REPO / "oracle" / "_ref" / "tessera_encode_ref"
-        if binary.exists():
-            threads = os.cpu_count() or 1
-            k, _ = cpu_sample_px(binary, tile, weights, work, threads, target_s=15.0)
-            pix = np.sort(np.random.default_rng(8).choice(total_px, size=k, replace=False))
-            wall, _ = run_ref_driver(binary, tile, pix, weights, work, threads)
-            cpu = {"value": k / wall, "unit": UNIT, "cores": threads, "kind": "port",
-                   "sample": f"{k} random pixels of the config-1 tile as a 1x{k} tile through the reference driver "
-                             f"(unmodified) + C++ restatement of the oneDNN CPU back end, {wall:.1f} s",
-                   "cpu_model": cpu_model()}
+        cpu = cpu_baseline_leg(tile, weights, work, target_s=20.0)
+    gpu_ref = None
+    if world == 1 and args.config == 1 and not args.no_gpu_reference:
+        gpu_ref = gpu_reference_leg(tile, weights, work)
     out = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": dev_ms_max / args.steps, "higher_is_better": True,
@@ -425,9 +511,14 @@ def main():
                                  for k, v in st["gemm_kind"].items()},
         "clocks": clocks.summary(),
         "outputs_match_e2e": ok,
+        "per_rank_ms": [r[0] / args.steps for r in per_rank],
+        "per_rank_e2e_ms": [r[1] / args.steps if r[1] >= 0 else None for r in per_rank],
+        "band_rows": [[int(r[2]), int(r[3])] for r in per_rank],
     }
     if cpu:
         out["cpu_baseline"] = cpu
+    if gpu_ref:
+        out["gpu_reference"] = gpu_ref
     print(json.dumps(out), flush=True)
     if dist is not None:
         dist.destroy_process_group()

@@ -239,7 +239,7 @@ struct Ctx {
     std::vector<uint16_t> pe_table;  // 367 x 640
     std::string dump_dir;
     int64_t dump_n = 0;
-    int64_t P = 8;                   // pixels per thread block
+    int64_t P = 8;                   // pixels per thread block (TC_BLOCK_S2, else TC_BLOCK)
     double wall = 0;
     uint64_t calls = 0, pixels = 0;
 };
@@ -349,10 +349,18 @@ void dump_call(Ctx &c, const float *s2, int64_t G, int64_t T2, const float *s1, 
 
 extern "C" {
 
-void *tc_create(const char *weights_path, int /*block_pixels*/) {
+void *tc_create(const char *weights_path, int block_pixels) {
     try {
         auto W = load_weights(weights_path);
-        auto *c = new Ctx();
+        auto c = std::make_unique<Ctx>();
+        // the reference's block sizes (tessera_cpu.cpp:486-489): TC_BLOCK pixels
+        // (block_pixels, default 4), TC_BLOCK_S2 a multiple of it (default the
+        // same). Pixels are independent, so they set only the work granularity
+        // of the thread loop, never a result.
+        const int64_t P1 = block_pixels > 0 ? block_pixels : 4;
+        const char *b2 = std::getenv("TC_BLOCK_S2");
+        c->P = b2 && std::atoi(b2) > 0 ? std::atoi(b2) : P1;
+        if (c->P % P1) throw std::runtime_error("TC_BLOCK_S2 must be a multiple of TC_BLOCK");
         init_backbone(W, c->bb[0], "s2_backbone", 10);
         init_backbone(W, c->bb[1], "s1_backbone", 2);
         c->red1 = take_linear(W, "dim_reducer.0.weight", "dim_reducer.0.bias");
@@ -367,7 +375,7 @@ void *tc_create(const char *weights_path, int /*block_pixels*/) {
                 c->pe_table[d * D + 2 * i + 1] = f2bf(std::cos(a));
             }
         if (const char *e = std::getenv("TC_ORACLE_DUMP")) c->dump_dir = e;
-        return c;
+        return c.release();
     } catch (const std::exception &e) {
         std::fprintf(stderr, "tc_create: %s\n", e.what());
         return nullptr;

@@ -717,7 +717,7 @@ __global__ void __launch_bounds__(256) k_layernorm640(const bf16 *__restrict__ x
     __shared__ __align__(16) float gs[D], bs[D];
     for (int i = threadIdx.x; i < D; i += blockDim.x) {
         gs[i] = g ? g[i] : 1.f;
-        bs[i] = g ? b[i] : 0.f;
+        bs[i] = b ? b[i] : 0.f;
     }
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -944,218 +944,6 @@ void launch_emb1(int C, const float *rec, int64_t M, const float *w1t, const flo
     check_launch("k_emb1");
 }
 
-// Persistent, software-pipelined attention: each CTA loops over (pixel, head)
-// items; while its warps compute item i from one K/V buffer, cp.async fills the
-// other with item i + grid, and each warp prefetches the next item's Q
-// fragments into registers. Same arithmetic as k_attention.
-template <int NTMAX>
-__device__ __forceinline__ void attn_rowblock(const uint32_t (&qa)[HD / 16][4], uint32_t ks_base, uint32_t vs_base,
-                                              int T, int rb, int lane, float scale, bf16 *__restrict__ att_head,
-                                              int64_t t0) {
-    const int g = lane >> 2, tq = lane & 3;
-    const int Tpad = (T + 15) & ~15;
-    const int nrb = Tpad / 16, nnt = Tpad / 8;
-    const int r0 = rb * 16 + g, r1 = r0 + 8;
-    uint32_t sp[NTMAX][2];
-#pragma unroll
-    for (int nt0 = 0; nt0 < NTMAX; nt0 += 4) {
-        if (nt0 < nnt) {
-            float c[4][4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) c[j][0] = c[j][1] = c[j][2] = c[j][3] = 0.f;
-#pragma unroll
-            for (int ks = 0; ks < HD / 16; ks += 2) {
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    if (nt0 + j < nnt) {
-                        const uint32_t addr =
-                            ks_base + (uint32_t)((((nt0 + j) * 8 + (lane & 7)) * ATT_LD + (lane >> 3) * 8 + ks * 16) * 2);
-                        uint32_t b0, b1, b2, b3;
-                        ldsm_x4(addr, b0, b1, b2, b3);
-                        mma_bf16_16816(c[j], qa[ks], b0, b1);
-                        mma_bf16_16816(c[j], qa[ks + 1], b2, b3);
-                    }
-                }
-            }
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                if (nt0 + j < NTMAX) {
-                    const int col = (nt0 + j) * 8 + 2 * tq;
-                    const float ninf = -INFINITY;
-                    const float s0 = col < T ? c[j][0] * scale : ninf, s1 = col + 1 < T ? c[j][1] * scale : ninf;
-                    const float s2 = col < T ? c[j][2] * scale : ninf, s3 = col + 1 < T ? c[j][3] * scale : ninf;
-                    sp[nt0 + j][0] = pack_bf16x2(s0, s1);
-                    sp[nt0 + j][1] = pack_bf16x2(s2, s3);
-                }
-            }
-        }
-    }
-    float mx0 = -INFINITY, mx1 = -INFINITY;
-#pragma unroll
-    for (int nt = 0; nt < NTMAX; ++nt)
-        if (nt < nnt) {
-            mx0 = fmaxf(mx0, fmaxf(bf16lo(sp[nt][0]), bf16hi(sp[nt][0])));
-            mx1 = fmaxf(mx1, fmaxf(bf16lo(sp[nt][1]), bf16hi(sp[nt][1])));
-        }
-#pragma unroll
-    for (int o = 1; o <= 2; o <<= 1) {
-        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
-        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
-    }
-    float z0 = 0.f, z1 = 0.f;
-#pragma unroll
-    for (int nt = 0; nt < NTMAX; ++nt)
-        if (nt < nnt) {
-            z0 += expf(bf16lo(sp[nt][0]) - mx0) + expf(bf16hi(sp[nt][0]) - mx0);
-            z1 += expf(bf16lo(sp[nt][1]) - mx1) + expf(bf16hi(sp[nt][1]) - mx1);
-        }
-#pragma unroll
-    for (int o = 1; o <= 2; o <<= 1) {
-        z0 += __shfl_xor_sync(0xffffffffu, z0, o);
-        z1 += __shfl_xor_sync(0xffffffffu, z1, o);
-    }
-    const float inv0 = 1.f / z0, inv1 = 1.f / z1;
-#pragma unroll
-    for (int nt = 0; nt < NTMAX; ++nt)
-        if (nt < nnt) {
-            sp[nt][0] = pack_bf16x2(expf(bf16lo(sp[nt][0]) - mx0) * inv0, expf(bf16hi(sp[nt][0]) - mx0) * inv0);
-            sp[nt][1] = pack_bf16x2(expf(bf16lo(sp[nt][1]) - mx1) * inv1, expf(bf16hi(sp[nt][1]) - mx1) * inv1);
-        }
-    uint32_t *dst0 = r0 < T ? reinterpret_cast<uint32_t *>(att_head + (t0 + r0) * D) : nullptr;
-    uint32_t *dst1 = r1 < T ? reinterpret_cast<uint32_t *>(att_head + (t0 + r1) * D) : nullptr;
-#pragma unroll
-    for (int half = 0; half < 2; ++half) {
-        float o[HD / 16][4];
-#pragma unroll
-        for (int dn = 0; dn < HD / 16; ++dn) o[dn][0] = o[dn][1] = o[dn][2] = o[dn][3] = 0.f;
-#pragma unroll
-        for (int kt = 0; kt < NTMAX / 2; ++kt) {
-            if (kt < nrb) {
-                const uint32_t a[4] = {sp[2 * kt][0], sp[2 * kt][1], sp[2 * kt + 1][0], sp[2 * kt + 1][1]};
-                const int vrow = kt * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
-                const uint32_t addr = vs_base + (uint32_t)((vrow * ATT_LD + half * (HD / 2) + (lane >> 4) * 8) * 2);
-#pragma unroll
-                for (int dn2 = 0; dn2 < HD / 32; ++dn2) {
-                    uint32_t b0, b1, b2, b3;
-                    ldsm_x4_t(addr + dn2 * 32, b0, b1, b2, b3);
-                    mma_bf16_16816(o[2 * dn2], a, b0, b1);
-                    mma_bf16_16816(o[2 * dn2 + 1], a, b2, b3);
-                }
-            }
-        }
-        if (dst0) {
-#pragma unroll
-            for (int dn = 0; dn < HD / 16; ++dn) dst0[half * (HD / 4) + dn * 4 + tq] = pack_bf16x2(o[dn][0], o[dn][1]);
-        }
-        if (dst1) {
-#pragma unroll
-            for (int dn = 0; dn < HD / 16; ++dn) dst1[half * (HD / 4) + dn * 4 + tq] = pack_bf16x2(o[dn][2], o[dn][3]);
-        }
-    }
-}
-
-__device__ __forceinline__ void attn_load_q(uint32_t (&qa)[HD / 16][4], const bf16 *__restrict__ qkv, int64_t t0, int T,
-                                            int h, int rb, int lane) {
-    const int g = lane >> 2, tq = lane & 3;
-    const int r0 = rb * 16 + g, r1 = r0 + 8;
-    const uint32_t *q0 = r0 < T ? reinterpret_cast<const uint32_t *>(qkv + (t0 + r0) * (3 * D) + h * HD) : nullptr;
-    const uint32_t *q1 = r1 < T ? reinterpret_cast<const uint32_t *>(qkv + (t0 + r1) * (3 * D) + h * HD) : nullptr;
-#pragma unroll
-    for (int ks = 0; ks < HD / 16; ++ks) {
-        qa[ks][0] = q0 ? __ldg(q0 + ks * 8 + tq) : 0u;
-        qa[ks][1] = q1 ? __ldg(q1 + ks * 8 + tq) : 0u;
-        qa[ks][2] = q0 ? __ldg(q0 + ks * 8 + 4 + tq) : 0u;
-        qa[ks][3] = q1 ? __ldg(q1 + ks * 8 + 4 + tq) : 0u;
-    }
-}
-
-template <int NTMAX>
-__global__ void __launch_bounds__(256, 1)
-    k_attention_pipe(const bf16 *__restrict__ qkv, Segs segs, int64_t nitems, bf16 *__restrict__ att, float scale) {
-    extern __shared__ __align__(16) uint8_t att_smem[];
-    constexpr int TP = 8 * NTMAX;                                  // rows per staged K or V buffer
-    bf16 *buf_base = reinterpret_cast<bf16 *>(att_smem);          // [2 buffers][K, V][TP][ATT_LD]
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
-    auto info = [&](int64_t it, int64_t &t0, int &T, int &h) {
-        const int64_t px = seg_pix(segs, it >> 2);
-        h = (int)(it & 3);
-        t0 = seg_at(segs, px);
-        T = (int)(seg_at(segs, px + 1) - t0);
-    };
-    auto stage = [&](int64_t it, int b) {
-        int64_t t0;
-        int T, h;
-        info(it, t0, T, h);
-        if (T <= 0) return;
-        const int Tpad = (T + 15) & ~15;
-        bf16 *Ks = buf_base + (size_t)b * 2 * TP * ATT_LD, *Vs = Ks + TP * ATT_LD;
-        const uint32_t ks = smem_u32(Ks), vs = smem_u32(Vs);
-        for (int idx = threadIdx.x; idx < Tpad * (HD / 8); idx += blockDim.x) {
-            const int r = idx / (HD / 8), c = idx % (HD / 8);
-            const uint32_t off = (uint32_t)((r * ATT_LD + c * 8) * 2);
-            if (r < T) {
-                const bf16 *row = qkv + (t0 + r) * (3 * D) + h * HD + c * 8;
-                cp_async16(ks + off, row + D);
-                cp_async16(vs + off, row + 2 * D);
-            } else {
-                *reinterpret_cast<uint4 *>(Ks + r * ATT_LD + c * 8) = make_uint4(0, 0, 0, 0);
-                *reinterpret_cast<uint4 *>(Vs + r * ATT_LD + c * 8) = make_uint4(0, 0, 0, 0);
-            }
-        }
-    };
-    int64_t it = blockIdx.x;
-    if (it < nitems) stage(it, 0);
-    asm volatile("cp.async.commit_group;" ::: "memory");
-    uint32_t qa[HD / 16][4];
-    if (it < nitems) {
-        int64_t t0;
-        int T, h;
-        info(it, t0, T, h);
-        if (warp * 16 < T) attn_load_q(qa, qkv, t0, T, h, warp, lane);
-    }
-    for (int b = 0; it < nitems; it += gridDim.x, b ^= 1) {
-        const int64_t nx = it + gridDim.x;
-        if (nx < nitems) stage(nx, b ^ 1);
-        asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 1;" ::: "memory");
-        __syncthreads();
-        int64_t t0;
-        int T, h;
-        info(it, t0, T, h);
-        const int nrb = ((T + 15) & ~15) / 16;
-        bf16 *Ks = buf_base + (size_t)b * 2 * TP * ATT_LD;
-        const uint32_t ks = smem_u32(Ks), vs = smem_u32(Ks + TP * ATT_LD);
-        for (int rb = warp; rb < nrb; rb += nwarps) {
-            if (rb != warp) attn_load_q(qa, qkv, t0, T, h, rb, lane);
-            attn_rowblock<NTMAX>(qa, ks, vs, T, rb, lane, scale, att + h * HD, t0);
-        }
-        if (nx < nitems) {  // next item's first Q row block, in flight across the barrier
-            int64_t n0;
-            int nT, nh;
-            info(nx, n0, nT, nh);
-            if (warp * 16 < nT) attn_load_q(qa, qkv, n0, nT, nh, warp, lane);
-        }
-        __syncthreads();  // buffer b is free for the copies issued next iteration
-    }
-    asm volatile("cp.async.wait_group 0;" ::: "memory");
-}
-
-template <int NT> static void attention_pipe(const bf16 *qkv, Segs segs, int64_t npix, bf16 *att, cudaStream_t st) {
-    static int grid_per_dev[64] = {};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    const size_t smem = (size_t)2 * 2 * 8 * NT * ATT_LD * sizeof(bf16);
-    if (!grid_per_dev[dev & 63]) {
-        cudaFuncSetAttribute(k_attention_pipe<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        int per_sm = 0, sms = 0;
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_attention_pipe<NT>, 256, smem);
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        grid_per_dev[dev & 63] = std::max(1, per_sm) * std::max(1, sms);
-    }
-    const int64_t items = npix * NH;
-    const unsigned grid = (unsigned)std::min<int64_t>(items, grid_per_dev[dev & 63]);
-    k_attention_pipe<NT><<<grid, 256, smem, st>>>(qkv, segs, items, att, 1.f / std::sqrt((float)HD));
-}
-
 template <int NT> static void attention_nt(const bf16 *qkv, Segs segs, int64_t npix, int Tpad, bf16 *att,
                                           cudaStream_t st) {
     static bool attr[64] = {};
@@ -1173,18 +961,6 @@ template <int NT> static void attention_nt(const bf16 *qkv, Segs segs, int64_t n
     const int warps = std::min(NT == 24 ? 16 : 8, Tpad / 16);
     const dim3 grid((unsigned)npix, NH);
     k_attention<NT><<<grid, 32 * warps, smem, st>>>(qkv, segs, att, 1.f / std::sqrt((float)HD));
-}
-
-// TC_ATTN_PIPE=1 selects the persistent pipelined kernel instead of one CTA
-// per (pixel, head). Off by default: on config 1 it took 1.71 s per tile
-// against 1.43 s, since its fixed 8 warps per SM leave warps idle on short
-// series where the per-item kernel packs more CTAs per SM.
-static bool attention_pipelined() {
-    static const bool on = [] {
-        const char *e = std::getenv("TC_ATTN_PIPE");
-        return e && *e == '1';
-    }();
-    return on;
 }
 
 // TC_ATTN_TC: 0 = always the mma.sync kernel, 1 (default) = the tcgen05 kernel
@@ -1227,7 +1003,6 @@ static void attention_tc(const bf16 *qkv, Segs segs, int64_t npix, int64_t ntok,
 
 int attention_class(int T) {
     if (T > 128) return 2;
-    if (attention_pipelined()) return 0;
     const int mode = attention_tcgen05();
     return mode == 2 || (mode == 1 && T > AT_MMA_MAX_T) ? 1 : 0;
 }
@@ -1256,14 +1031,6 @@ static void attention_of_class(int cls, const bf16 *qkv, Segs segs, int64_t npix
     const int Tpad = (tmax + 15) & ~15;
     if (cls == 1) {
         attention_tc(qkv, segs, npix, ntok, att, status, st);
-    } else if (attention_pipelined()) {
-        if (Tpad <= 32) attention_pipe<4>(qkv, segs, npix, att, st);
-        else if (Tpad <= 64) attention_pipe<8>(qkv, segs, npix, att, st);
-        else if (Tpad <= 96) attention_pipe<12>(qkv, segs, npix, att, st);
-        else if (Tpad <= 128) attention_pipe<16>(qkv, segs, npix, att, st);
-        // two K/V buffers of more than 128 rows do not fit in shared memory
-        else if (Tpad <= 192) attention_nt<24>(qkv, segs, npix, Tpad, att, st);
-        else attention_nt<32>(qkv, segs, npix, Tpad, att, st);
     } else {
         if (Tpad <= 32) attention_nt<4>(qkv, segs, npix, Tpad, att, st);
         else if (Tpad <= 64) attention_nt<8>(qkv, segs, npix, Tpad, att, st);

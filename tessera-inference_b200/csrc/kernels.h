@@ -53,8 +53,7 @@ void launch_emb1(int C, const float *rec, int64_t M, const float *w1t, const flo
 // The kernel for a pixel is chosen by that pixel's own series length T, so a
 // pixel's result never depends on which other pixels share its chunk (row
 // bands, devices and the tc_encode batches all give the same bytes):
-//   class 0: the mma.sync kernel, for T <= 48 (every T <= 128 with TC_ATTN_TC=0
-//            or TC_ATTN_PIPE=1);
+//   class 0: the mma.sync kernel, for T <= 48 (every T <= 128 with TC_ATTN_TC=0);
 //   class 1: the tcgen05 kernel, for 48 < T <= 128 (every T <= 128 with
 //            TC_ATTN_TC=2); its bounded waits report into *status (may be null);
 //   class 2: the mma.sync kernel, for T > 128.

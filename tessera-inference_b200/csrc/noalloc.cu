@@ -90,12 +90,14 @@ extern "C" int tcb_op_gemm_ln_noalloc(const void *A, int lda, const void *W, con
         p.status = status;
         launch_gemm(p, static_cast<const bf16 *>(A), lda, static_cast<const bf16 *>(W), st, 0, 0, 1);
         launch_layernorm640(y, M, ln_g, ln_b, static_cast<bf16 *>(out), st);
-        // synchronous, so a device-side error is reported by this call
+        // the status word is read back on the caller's stream, behind the two
+        // kernels, and one wait on that stream covers all three: no other
+        // stream of the device is waited for
+        int s = 0;
+        e = cudaMemcpyAsync(&s, status, sizeof(int), cudaMemcpyDeviceToHost, st);
+        if (e != cudaSuccess) throw std::runtime_error(std::string("status read: ") + cudaGetErrorString(e));
         e = cudaStreamSynchronize(st);
         if (e != cudaSuccess) throw std::runtime_error(std::string("stream: ") + cudaGetErrorString(e));
-        int s = 0;
-        e = cudaMemcpy(&s, status, sizeof(int), cudaMemcpyDeviceToHost);
-        if (e != cudaSuccess) throw std::runtime_error(std::string("status read: ") + cudaGetErrorString(e));
         if (s != 0) throw std::runtime_error("device status " + std::to_string(s));
         return 0;
     } catch (const std::exception &ex) {

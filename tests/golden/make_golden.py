@@ -18,6 +18,12 @@
       ref_api.json: the tokens of the four back-end prototypes
       (tc_create / tc_encode / tc_profile_dump / tc_destroy) as the reference
       driver declares them (src/tessera_encode.cpp:47-52).
+  python tests/golden/make_golden.py subsets [CFG ...]
+      cfg1_subset.npz, cfg3_subset.npz, cfg4_subset.npz: a stratified pixel
+      subset of the full-size benchmark tiles of configs 1, 3 and 4 (every
+      (bin2, bin1) key, the empty and few-step pixels, the first and last
+      pixel of every row band and every chunk) and the reference driver's
+      codes and scales for those pixels (minutes on a few cores).
   python tests/golden/make_golden.py refcuda       (on a B200)
       Runs the reference's unmodified driver + CUDA back end
       (oracle/_ref/tessera_encode_cuda_ref, built by `make -C oracle cuda-ref`)
@@ -160,6 +166,84 @@ def refcuda():
             print(name, codes.shape)
 
 
+# config -> (pixels sampled per (bin2, bin1) key, row-band splits whose band
+# and chunk boundaries are covered). Config 4 runs one whole tile per GPU.
+SUBSETS = {1: (150, (1, 2, 4, 8)), 3: (150, (1, 2, 4, 8)), 4: (100, (1,))}
+# the library's default chunk caps (TC_CHUNK_TOKENS, TC_CHUNK_PIXELS)
+CHUNK_TOKENS, CHUNK_PIXELS = 524288, 32768
+
+
+def chunk_starts(t2: np.ndarray, t1: np.ndarray, tok_cap: int = CHUNK_TOKENS, px_cap: int = CHUNK_PIXELS):
+    """First pixel (relative to the band) of every chunk the library's planner
+    cuts a band into: each chunk takes pixels while it holds at most px_cap
+    pixels and tok_cap tokens of either modality (encode_band in
+    tessera-inference_b200/csrc/backend.cu)."""
+    o2 = np.concatenate([[0], np.cumsum(t2)])
+    o1 = np.concatenate([[0], np.cumsum(t1)])
+    n, i0, starts = len(t2), 0, []
+    while i0 < n:
+        starts.append(i0)
+        a = int(np.searchsorted(o2, o2[i0] + tok_cap, side="right")) - 1
+        b = int(np.searchsorted(o1, o1[i0] + tok_cap, side="right")) - 1
+        i1 = min(n, i0 + px_cap, a, b)
+        if i1 <= i0:
+            raise ValueError("a pixel larger than the token cap")
+        i0 = i1
+    return starts
+
+
+def subset_pixels(cfg: int, tile: dict) -> np.ndarray:
+    """The stratified pixel subset of a benchmark configuration: a seeded sample
+    of every (bin2, bin1) key present (the pixels with no observation, key 0,
+    and the one-modality and few-step keys included), plus the first and last
+    pixel of every row band of each split and of every chunk of each band."""
+    import oracle
+    import tessera_b200 as tb
+    per_key, splits = SUBSETS[cfg]
+    T2, H, W = tile["masks"].shape
+    n2, n1 = oracle.counts(tile)
+    key = oracle.bin_size(n2) * 1000 + oracle.bin_size(n1)
+    rng = np.random.default_rng(100 + cfg)
+    pick = []
+    for k in np.unique(key):
+        idx = np.flatnonzero(key == k)
+        pick.append(rng.choice(idx, size=min(per_key, idx.size), replace=False))
+    t2, t1 = oracle.tile_tokens(tile)
+    for nb in splits:
+        rows = tb.plan_rows(tile, nb) if nb > 1 else [0, H]
+        for r0, r1 in zip(rows, rows[1:]):
+            p0, p1 = r0 * W, r1 * W
+            if p1 <= p0:
+                continue
+            s = np.array(chunk_starts(t2[p0:p1], t1[p0:p1]), np.int64) + p0
+            pick += [s, s[1:] - 1, np.array([p1 - 1], np.int64)]
+    return np.unique(np.concatenate(pick)).astype(np.int64)
+
+
+def subsets(cfgs=(1, 3, 4)):
+    """<cfgN>_subset.npz: for configs 1, 3 and 4, the stratified pixel subset
+    (subset_pixels) and the codes and scales the reference's unmodified driver
+    with the CPU back-end restatement writes for those pixels, run as one 1 x K
+    tile (exact: every pixel's result depends only on its own series)."""
+    binary = REPO / "oracle" / "_ref" / "tessera_encode_ref"
+    if not binary.exists():
+        sys.exit("build the reference driver first: make -C oracle")
+    with tempfile.TemporaryDirectory() as td:
+        w = synth.make_weights(Path(td) / "w.tcw", seed=0)
+        for cfg in cfgs:
+            tile = synth.make_config_tile(cfg)
+            pix = subset_pixels(cfg, tile)
+            sub = synth.subset_tile(tile, pix)
+            del tile
+            tdir = synth.write_tile_dir(sub, Path(td) / f"grid_cfg{cfg}")
+            out = Path(td) / "out"
+            r = subprocess.run([str(binary), str(tdir), str(out), str(w)], check=True, capture_output=True, text=True)
+            codes = np.load(out / f"grid_cfg{cfg}.npy").reshape(-1, 128)
+            scales = np.load(out / f"grid_cfg{cfg}_scales.npy").reshape(-1)
+            np.savez_compressed(HERE / f"cfg{cfg}_subset.npz", pixels=pix, codes=codes, scales=scales)
+            print(f"cfg{cfg}: {pix.size} px;", r.stdout.strip().splitlines()[0])
+
+
 API_NAMES = ("tc_create", "tc_encode", "tc_profile_dump", "tc_destroy")
 
 
@@ -224,3 +308,5 @@ if __name__ == "__main__":
         api()
     if cmd == "refcuda":
         refcuda()
+    if cmd == "subsets":
+        subsets(tuple(int(c) for c in sys.argv[2:]) or (1, 3, 4))

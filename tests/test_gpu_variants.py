@@ -1,7 +1,7 @@
 """Opt-in kernel variants, each in a subprocess with its environment switch
-(the library reads TC_ATTN_PIPE, TC_ATTN_TC, TC_LN_FUSE and TC_GEMM_VARIANT
-once at load): whole-tile parity against the oracle golden for the pipelined
-attention, the mma.sync attention on every chunk (TC_ATTN_TC=0), the tcgen05
+(the library reads TC_ATTN_TC, TC_LN_FUSE and TC_GEMM_VARIANT once at load):
+whole-tile parity against the oracle golden for the mma.sync attention on
+every chunk (TC_ATTN_TC=0), the tcgen05
 attention on every chunk of series up to 128 steps, short ones included
 (TC_ATTN_TC=2), the LayerNorm-fused GEMM epilogue and the CTA-pair
 (cta_group::2) GEMM."""
@@ -33,7 +33,7 @@ assert_acceptance(m)
 """
 
 
-@pytest.mark.parametrize("env", [{"TC_ATTN_PIPE": "1"}, {"TC_ATTN_TC": "0"}, {"TC_ATTN_TC": "2"},
+@pytest.mark.parametrize("env", [{"TC_ATTN_TC": "0"}, {"TC_ATTN_TC": "2"},
                                  {"TC_LN_FUSE": "1"}, {"TC_GEMM_VARIANT": "2"}])
 def test_variant_parity(env):
     code = CODE.format(pkg=str(REPO / "tessera-inference_b200"), orc=str(REPO / "oracle"), tests=str(REPO / "tests"))

@@ -66,3 +66,18 @@ def test_noalloc_rejects_oversize(capfd):
     rc = lib.tcb_op_gemm_ln_noalloc(1, 640, 1, None, None, 640, 1, 1, 1, 8193, 640, None)
     assert rc == -1
     assert "8192" in capfd.readouterr().err
+
+
+def test_noalloc_after_a_refused_call(capfd):
+    """A call the GEMM refuses (K = 100 is not a multiple of 64) returns -1;
+    the next valid call starts from a cleared status word and matches the
+    existing entry point."""
+    lib = tb.load_library()
+    A, W, bias, res, gam, bet = _case(64, 640, 3)
+    out = torch.empty(64, 640, device="cuda", dtype=torch.bfloat16)
+    st = torch.cuda.current_stream().cuda_stream
+    rc = lib.tcb_op_gemm_ln_noalloc(A.data_ptr(), 100, W.data_ptr(), bias.data_ptr(), res.data_ptr(), 640,
+                                    gam.data_ptr(), bet.data_ptr(), out.data_ptr(), 64, 100, st)
+    assert rc == -1
+    assert "multiple of 64" in capfd.readouterr().err
+    _both(lib, 64, 640, 3)
