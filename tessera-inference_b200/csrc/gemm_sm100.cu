@@ -246,79 +246,6 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs &p, uint32_t tbase,
     return true;
 }
 
-// Tile index of the tl-th tile a CTA works on. Plain: tiles blockIdx.x,
-// blockIdx.x + gridDim.x, ... (row block t / num_n, column tile t % num_n).
-// Whole rows (ROWLN): every column tile of row blocks blockIdx.x,
-// blockIdx.x + gridDim.x, ... in column order, so one CTA writes all of a
-// row block's output before it moves on.
-template <bool ROWLN> __device__ __forceinline__ int tile_at(int tl, int num_n) {
-    if constexpr (ROWLN) return ((int)blockIdx.x + (tl / num_n) * (int)gridDim.x) * num_n + tl % num_n;
-    else return (int)blockIdx.x + tl * (int)gridDim.x;
-}
-
-__device__ __forceinline__ float warp_allsum(float v) {
-#pragma unroll
-    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    return v;
-}
-
-// Row-pass LayerNorm of a finished row block: epilogue warp e normalises rows
-// m0 + e, m0 + e + 8, ... of y = p.out (N = 640, just written by this CTA, so
-// read from L2) into p.ln_rows_out, with the arithmetic of k_layernorm640:
-// lane l holds columns 128 j + 4 l .. + 3, two-pass f32 mean and biased
-// variance, rstd = 1 / sqrtf(var + 1e-5), out = (y - mean) rstd g + b rounded
-// to bf16. The next row is loaded before the current one is reduced. Once a
-// row is normalised, its y lines are dropped from L2 without being written
-// back (discard.global.L2): y is dead, so it need never reach HBM.
-__device__ __forceinline__ void ln_rowpass(const GemmArgs &p, int m0, int e, int lane, const float *gs,
-                                           const float *bs) {
-    constexpr int ROWS = BM / EPI_WARPS;
-    auto load = [&](int r, uint2 (&q)[5]) {
-        const bf16 *yr = p.out + (size_t)r * p.ldo + lane * 4;
-#pragma unroll
-        for (int j = 0; j < 5; ++j) q[j] = __ldcg(reinterpret_cast<const uint2 *>(yr + j * 128));
-    };
-    uint2 q[5], qn[5];
-    int r = m0 + e;
-    if (r < p.M) load(r, q);
-#pragma unroll 1
-    for (int i = 0; i < ROWS && r < p.M; ++i, r += EPI_WARPS) {
-        if (i + 1 < ROWS && r + EPI_WARPS < p.M) load(r + EPI_WARPS, qn);
-        float s = 0.f;
-#pragma unroll
-        for (int j = 0; j < 5; ++j) {
-            s += bf16lo(q[j].x); s += bf16hi(q[j].x);
-            s += bf16lo(q[j].y); s += bf16hi(q[j].y);
-        }
-        const float mean = warp_allsum(s) / (float)D;
-        float ss = 0.f;
-#pragma unroll
-        for (int j = 0; j < 5; ++j) {
-            const float d0 = bf16lo(q[j].x) - mean, d1 = bf16hi(q[j].x) - mean;
-            const float d2 = bf16lo(q[j].y) - mean, d3 = bf16hi(q[j].y) - mean;
-            ss += d0 * d0; ss += d1 * d1; ss += d2 * d2; ss += d3 * d3;
-        }
-        const float rstd = 1.f / sqrtf(warp_allsum(ss) / (float)D + LN_EPS);
-        bf16 *orow = p.ln_rows_out + (size_t)r * p.ldo + lane * 4;
-#pragma unroll
-        for (int j = 0; j < 5; ++j) {
-            const int c = j * 128 + lane * 4;
-            const float4 gg = *reinterpret_cast<const float4 *>(gs + c), bb = *reinterpret_cast<const float4 *>(bs + c);
-            const uint32_t o0 = pack_bf16x2((bf16lo(q[j].x) - mean) * rstd * gg.x + bb.x,
-                                            (bf16hi(q[j].x) - mean) * rstd * gg.y + bb.y);
-            const uint32_t o1 = pack_bf16x2((bf16lo(q[j].y) - mean) * rstd * gg.z + bb.z,
-                                            (bf16hi(q[j].y) - mean) * rstd * gg.w + bb.w);
-            *reinterpret_cast<uint2 *>(orow + j * 128) = make_uint2(o0, o1);
-        }
-        if (p.ln_discard && lane < (D * 2) / 128) {
-            const bf16 *line = p.out + (size_t)r * p.ldo + lane * 64;
-            asm volatile("discard.global.L2 [%0], 128;" ::"l"(line) : "memory");
-        }
-#pragma unroll
-        for (int j = 0; j < 5; ++j) q[j] = qn[j];
-    }
-}
-
 // Column split of a w-wide tile between the two epilogue warps of a quadrant
 // (at a multiple of 32 near the middle).
 __host__ __device__ constexpr int epi_split(int w) { return ((w / 2 + 16) / 32) * 32; }
@@ -333,11 +260,7 @@ template <int BN> __host__ __device__ constexpr int epi_split() { return epi_spl
 // With a residual matrix, the producer also prefetches each tile's residual
 // block into L2 (tmR, boxes of 128 x 128) when it starts loading the tile, so
 // the epilogue's residual reads, a tile later, hit L2 instead of HBM.
-// ROWLN (N = 640 only): whole-row schedule (tile_at) and, after the last
-// column tile of each row block, the row-pass LayerNorm (ln_rowpass) of that
-// block into p.ln_rows_out. The epilogue warps meet on an mbarrier (bounded
-// wait) before the pass, so every column of the block is stored.
-template <int BN, bool ROWLN>
+template <int BN>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     k_gemm_bf16(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ CUtensorMap tmBt, const __grid_constant__ CUtensorMap tmR, GemmArgs p) {
@@ -352,9 +275,6 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     uint64_t *full = bars, *empty = bars + S, *tfull = bars + 2 * S, *tempty = bars + 2 * S + 2;
     uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 2 * S + 4);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
-    uint64_t *lnbar = bars + 2 * S + 5;                                        // ROWLN only
-    float *ln_gs = reinterpret_cast<float *>(staging + STAGING_BYTES + 256);   // ROWLN only: gamma, beta
-    float *ln_bs = ln_gs + D;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int num_n = (p.N + BN - 1) / BN;
@@ -366,19 +286,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     if (threadIdx.x == 0) {
         for (int i = 0; i < S; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 1); }
         for (int i = 0; i < 2; ++i) { mbar_init(&tfull[i], 1); mbar_init(&tempty[i], EPI_WARPS); }
-        if constexpr (ROWLN) mbar_init(lnbar, EPI_WARPS);
         *abort_flag = 0;
         fence_mbar_init();
         prefetch_tensormap(&tmA);
         prefetch_tensormap(&tmB);
         if (tail != BN) prefetch_tensormap(&tmBt);
         if (p.res) prefetch_tensormap(&tmR);
-    }
-    if constexpr (ROWLN) {
-        for (int i = threadIdx.x; i < D; i += blockDim.x) {
-            ln_gs[i] = p.ln_g[i];
-            ln_bs[i] = p.ln_b[i];
-        }
     }
     if (warp == 1) { tmem_alloc(tmem_holder, 512); tmem_relinquish(); }
     tc_fence_before();
@@ -390,9 +303,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         if (lane == 0) {
             int s = 0;
             uint32_t ph = 0;
-            for (int tl = 0;; ++tl) {
-                const int t = tile_at<ROWLN>(tl, num_n);
-                if (t >= ntiles) break;
+            for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
                 const int nt = t % num_n, m0 = (t / num_n) * BM, n0 = nt * BN;
                 const bool last = nt == num_n - 1;
                 const CUtensorMap *tb = last ? &tmBt : &tmB;
@@ -422,9 +333,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             const uint32_t idesc_tail = umma_idesc_bf16(BM, tail);
             int s = 0;
             uint32_t ph = 0;
-            for (int tl = 0;; ++tl) {
-                const int t = tile_at<ROWLN>(tl, num_n);
-                if (t >= ntiles) break;
+            int tl = 0;
+            for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++tl) {
                 const uint32_t idesc = t % num_n == num_n - 1 ? idesc_tail : idesc_full;
                 const int buf = tl & 1;
                 const uint32_t use = (uint32_t)(tl >> 1);
@@ -454,10 +364,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         // epilogue warps 2..9: TMEM lane quadrant = warp % 4, column half = (warp - 2) / 4
         const int quad = warp & 3, e = warp - 2, half = e >> 2;
         uint8_t *stage = staging + e * (32 * 64);
-        uint32_t lnph = 0;
-        for (int tl = 0;; ++tl) {
-            const int t = tile_at<ROWLN>(tl, num_n);
-            if (t >= ntiles) break;
+        int tl = 0;
+        for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++tl) {
             const int nt = t % num_n, m0 = (t / num_n) * BM, n0 = nt * BN;
             const int w = nt == num_n - 1 ? tail : BN;
             const int c0 = half ? epi_split(w) : 0, c1 = half ? w : epi_split(w);
@@ -467,17 +375,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             if (!epilogue_tile(p, tbase, m0 + quad * 32, n0, c0, c1, stage, lane, &tfull[buf], use & 1, abort_flag))
                 break;
             tc_fence_before();
-            __threadfence_block();  // this warp's y stores, before the row pass of other warps reads them
             __syncwarp();
             if (lane == 0) mbar_arrive(&tempty[buf]);
-            if constexpr (ROWLN) {
-                if (nt == num_n - 1) {
-                    if (lane == 0) mbar_arrive(lnbar);
-                    if (!mbar_wait(lnbar, lnph, abort_flag, p.status, ERR_WAIT_LN_EXCHANGE)) break;
-                    lnph ^= 1;
-                    ln_rowpass(p, m0, e, lane, ln_gs, ln_bs);
-                }
-            }
         }
     }
 
@@ -983,15 +882,14 @@ static int num_sms() {
     return n;
 }
 
-template <int BN, bool ROWLN = false>
-static void launch_bn(const GemmArgs &p, const bf16 *A, int lda, const bf16 *W, cudaStream_t st, int max_ctas) {
+template <int BN> static void launch_bn(const GemmArgs &p, const bf16 *A, int lda, const bf16 *W, cudaStream_t st,
+                                        int max_ctas) {
     using Cfg = GemmCfg<BN>;
-    constexpr int SMEM = Cfg::SMEM_BYTES + (ROWLN ? 2 * D * (int)sizeof(float) : 0);
     static bool attr_set[64] = {};  // per device
     int dev = 0;
     cudaGetDevice(&dev);
     if (!attr_set[dev & 63]) {
-        cudaError_t e = cudaFuncSetAttribute(k_gemm_bf16<BN, ROWLN>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+        cudaError_t e = cudaFuncSetAttribute(k_gemm_bf16<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
         if (e != cudaSuccess) throw std::runtime_error(std::string("gemm smem attribute: ") + cudaGetErrorString(e));
         attr_set[dev & 63] = true;
     }
@@ -1007,12 +905,11 @@ static void launch_bn(const GemmArgs &p, const bf16 *A, int lda, const bf16 *W, 
     make_tmap(&tb, W, (uint64_t)p.N, (uint64_t)p.K, (uint64_t)p.K, num_n == 1 ? (uint32_t)tail : (uint32_t)BN);
     if (tail != BN) make_tmap(&tbt, W, (uint64_t)p.N, (uint64_t)p.K, (uint64_t)p.K, (uint32_t)tail);
     else tbt = tb;
-    const int num_m = (p.M + BM - 1) / BM;
-    // whole-row schedule: a CTA owns row blocks, so the grid is capped by them
-    int grid = std::min(ROWLN ? num_m : num_m * num_n, num_sms());
+    const int ntiles = ((p.M + BM - 1) / BM) * num_n;
+    int grid = std::min(ntiles, num_sms());
     if (max_ctas > 0) grid = std::min(grid, max_ctas);
     if (grid < 1) grid = 1;
-    k_gemm_bf16<BN, ROWLN><<<grid, GEMM_THREADS, SMEM, st>>>(ta, tb, tbt, tr, p);
+    k_gemm_bf16<BN><<<grid, GEMM_THREADS, Cfg::SMEM_BYTES, st>>>(ta, tb, tbt, tr, p);
 }
 
 template <int BN> static void launch_pair(const GemmArgs &p, const bf16 *A, int lda, const bf16 *W, cudaStream_t st,
@@ -1095,15 +992,6 @@ void launch_gemm(const GemmArgs &p, const bf16 *A, int lda, const bf16 *W, cudaS
     if (bn == 0 || p.N % 16 || (variant == 2 && p.N % bn))
         throw std::runtime_error("gemm: unsupported N " + std::to_string(p.N));
     if (p.ldo % 8 || (p.res && p.ldr % 8)) throw std::runtime_error("gemm: output/residual pitch must be 16-byte aligned");
-    if (p.ln_rows_out) {
-        if (p.N != D || !p.ln_g || !p.ln_b || p.pe_doy || p.ldo != D)
-            throw std::runtime_error("gemm: the row-pass LayerNorm needs N = ldo = 640, gamma and beta");
-        GemmArgs q = p;
-        // y lines are dropped from L2 after the pass only when every row starts a 128-byte line
-        q.ln_discard = (reinterpret_cast<uintptr_t>(p.out) % 128 == 0) ? 1 : 0;
-        launch_bn<256, true>(q, A, lda, W, st, max_ctas);
-        return;
-    }
     if (p.ln_g) {
         if (p.N != LN_N || !p.ln_b || p.pe_doy) throw std::runtime_error("gemm: LayerNorm epilogue needs N = 640");
         launch_ln(p, A, lda, W, st);

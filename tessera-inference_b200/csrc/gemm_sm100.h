@@ -30,14 +30,6 @@ struct GemmArgs {
     // epilogue of a 4-CTA cluster (one 160-column tile per CTA).
     const float *ln_g = nullptr;
     const float *ln_b = nullptr;
-    // When set (N = ldo = 640, with ln_g and ln_b): the row-pass LayerNorm.
-    // The GEMM writes y = out as usual and, once a CTA has stored every column
-    // of a 128-row block, its epilogue warps normalise those rows into
-    // ln_rows_out = bf16(LayerNorm(y) * ln_g + ln_b) (the arithmetic of the
-    // LayerNorm kernel) and drop y's lines from L2 unwritten: y is scratch,
-    // its contents undefined after the call.
-    __nv_bfloat16 *ln_rows_out = nullptr;
-    int ln_discard = 0;  // set by launch_gemm
 };
 
 // 2-D bf16 tensor map over a row-major [rows, cols] matrix with row pitch
