@@ -51,13 +51,14 @@ import synth  # noqa: E402
 METRIC = "pixels/sec (tiles/hour) per B200 and whole box at 1/2/4/8 GPUs vs ref CPU"
 UNIT = "px/s"
 WORKLOAD = "config 1: synthetic Manchester-sized tile 1113x695 (773,535 px), T2=120 (60% valid), Ta=Td=60"
-# DRAM bytes per GEMM FLOP (dram__bytes_read.sum + dram__bytes_write.sum summed
-# over all 360 k_gemm_bf16 launches of one ncu capture of five config-0 encodes:
-# 126.5 GB for 58.9 TFLOP), and the algorithmic bytes per FLOP of the layer mix
-# (per token and layer QKV 5120 B, out-proj 3840 B, FFN1 6400 B, FFN2 7680 B over
-# 9.83 MFLOP).
-GEMM_DRAM_BYTES_PER_FLOP = 2.15e-3
-GEMM_ALG_BYTES_PER_FLOP = 2.34e-3
+# DRAM bytes per GEMM FLOP: dram__bytes_read.sum + dram__bytes_write.sum summed
+# over the 1,587 GEMM launches of one ncu capture of a config-1 band (64 rows of
+# a tile with config 1's series and value distributions; 832.8 GB for 3.751e14
+# FLOP; profiles/launch_list_config1_band.md), and the algorithmic bytes per
+# FLOP of the same launches (per token emb2 2,560 B and per layer QKV 5,120 B,
+# out-proj 3,840 B, FFN1 6,400 B, FFN2 7,680 B; 8.851e11 B).
+GEMM_DRAM_BYTES_PER_FLOP = 2.22e-3
+GEMM_ALG_BYTES_PER_FLOP = 2.36e-3
 SMI_FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -501,8 +502,9 @@ def main():
                      "traffic": (GEMM_DRAM_BYTES_PER_FLOP * st["gemm_flop"] / st["gemm_launches"]
                                  if st.get("gemm_launches") else None),
                      "traffic_unit": "DRAM bytes per GEMM launch",
-                     "traffic_source": "ncu capture of every GEMM launch of config 0 (DRAM bytes per FLOP), "
-                                       "scaled by this run's FLOP per launch",
+                     "traffic_source": "ncu DRAM bytes per FLOP of every GEMM launch of a config-1 band "
+                                       "(profiles/launch_list_config1_band.md), scaled by this run's FLOP per "
+                                       "launch",
                      "algorithmic_bytes_per_launch": (GEMM_ALG_BYTES_PER_FLOP * st["gemm_flop"] / st["gemm_launches"]
                                                       if st.get("gemm_launches") else None),
                      "end_to_end_tflops": alg_tflops, "end_to_end_frac": alg_tflops / peak},

@@ -33,20 +33,6 @@ int tcb_op_gemm(const void *A, int lda, const void *W, const float *bias, int re
 int tcb_op_gemm_ln(const void *A, int lda, const void *W, const float *bias, const void *res, int ldr,
                    const float *ln_g, const float *ln_b, void *out, int ldo, int M, int K, int *status, void *stream);
 
-/* GEMM + residual + LayerNorm as the back end runs LN1 / LN2 (replaces the
- * reference's out-proj + LN1 and FFN2 + LN2, src/tessera_cpu.cpp:424-428 and
- * 245-263; src/tessera_cuda.cu:561-569): y = bf16(A W^T + bias + res) is
- * written to the caller's scratch y (M x 640, pitch 640), and once a CTA has
- * stored all 640 columns of a 128-row block it normalises those rows into
- * out = bf16(LayerNorm(y) * ln_g + ln_b), eps 1e-5 (pitch 640), with the
- * arithmetic of tcb_op_layernorm640, so out is bit-identical to
- * tcb_op_gemm + tcb_op_layernorm640. y's contents are undefined afterwards
- * (its cache lines are dropped, not written back). Bounded waits report into
- * *status. Asynchronous on `stream`. */
-int tcb_op_gemm_ln_rows(const void *A, int lda, const void *W, const float *bias, const void *res, int ldr,
-                        const float *ln_g, const float *ln_b, void *y, void *out, int M, int K, int *status,
-                        void *stream);
-
 /* Allocation-free form of tcb_op_gemm_ln, with no counterpart in the
  * reference. For callers that may not allocate device memory, such as a plugin
  * whose host framework owns the whole device-memory budget, or a hot path

@@ -341,7 +341,7 @@ enum GemmKind { GK_EMB2 = 0, GK_QKV, GK_OUT, GK_FFN1, GK_FFN2, GK_HEAD };
 
 static void gemm(Dev &d, int kind, const Lin &L, const bf16 *A, int64_t M, bf16 *out, bool relu,
                  const bf16 *res = nullptr, const float *pe_doy = nullptr, int pe_stride = 1,
-                 const float *ln_g = nullptr, const float *ln_b = nullptr, bf16 *ln_rows_out = nullptr) {
+                 const float *ln_g = nullptr, const float *ln_b = nullptr) {
     if (M <= 0) return;
     d.mark(100 + kind);
     GemmArgs p;
@@ -361,7 +361,6 @@ static void gemm(Dev &d, int kind, const Lin &L, const bf16 *A, int64_t M, bf16 
     p.status = d.status.p;
     p.ln_g = ln_g;
     p.ln_b = ln_b;
-    p.ln_rows_out = ln_rows_out;
     launch_gemm(p, A, L.K, L.w, d.st);
     d.stats.gemm_flop += 2.0 * double(M) * L.N * L.K;
     d.stats.gemm_flop_kind[kind] += 2.0 * double(M) * L.N * L.K;
@@ -377,18 +376,6 @@ static bool ln_fused() {
     static const bool on = [] {
         const char *e = std::getenv("TC_LN_FUSE");
         return e && *e == '1';
-    }();
-    return on;
-}
-
-// LN1 / LN2 as a row pass inside the out-proj / FFN2 GEMMs (GemmArgs::
-// ln_rows_out), with the LayerNorm kernel's arithmetic, so the pre-LN rows y
-// are read back from L2 rather than HBM and never written back. TC_LN_ROWPASS=0
-// runs the separate LayerNorm kernel instead (the same bytes).
-static bool ln_rowpass() {
-    static const bool on = [] {
-        const char *e = std::getenv("TC_LN_ROWPASS");
-        return !(e && *e == '0');
     }();
     return on;
 }
@@ -413,11 +400,6 @@ static void backbone(Dev &d, int b, const float *rec, Segs segs, int64_t M, int 
                 gemm(d, GK_OUT, B.out[l], d.att.p, M, d.x1.p, false, d.x.p, nullptr, 1, B.ln1g[l], B.ln1b[l]);
                 gemm(d, GK_FFN1, B.ffn1[l], d.x1.p, M, d.hbuf.p, true);
                 gemm(d, GK_FFN2, B.ffn2[l], d.hbuf.p, M, d.x.p, false, d.x1.p, nullptr, 1, B.ln2g[l], B.ln2b[l]);
-            } else if (ln_rowpass()) {  // y -> x1 / x inside the GEMM, y never leaves the L2
-                gemm(d, GK_OUT, B.out[l], d.att.p, M, d.y.p, false, d.x.p, nullptr, 1, B.ln1g[l], B.ln1b[l], d.x1.p);
-                gemm(d, GK_FFN1, B.ffn1[l], d.x1.p, M, d.hbuf.p, true);
-                gemm(d, GK_FFN2, B.ffn2[l], d.hbuf.p, M, d.y.p, false, d.x1.p, nullptr, 1, B.ln2g[l], B.ln2b[l],
-                     d.x.p);
             } else {
                 gemm(d, GK_OUT, B.out[l], d.att.p, M, d.y.p, false, d.x.p);
                 d.mark(TC_CAT_LN);
@@ -988,20 +970,6 @@ int tcb_op_gemm_ln(const void *A, int lda, const void *W, const float *bias, con
         p.res = static_cast<const bf16 *>(res); p.ldr = ldr;
         p.out = static_cast<bf16 *>(out); p.ldo = ldo; p.status = status;
         p.ln_g = ln_g; p.ln_b = ln_b;
-        launch_gemm(p, static_cast<const bf16 *>(A), lda, static_cast<const bf16 *>(W),
-                    static_cast<cudaStream_t>(stream));
-    })
-}
-
-int tcb_op_gemm_ln_rows(const void *A, int lda, const void *W, const float *bias, const void *res, int ldr,
-                        const float *ln_g, const float *ln_b, void *y, void *out, int M, int K, int *status,
-                        void *stream) {
-    OP_TRY("tcb_op_gemm_ln_rows", {
-        GemmArgs p;
-        p.M = M; p.N = 640; p.K = K; p.bias = bias;
-        p.res = static_cast<const bf16 *>(res); p.ldr = ldr;
-        p.out = static_cast<bf16 *>(y); p.ldo = 640; p.status = status;
-        p.ln_g = ln_g; p.ln_b = ln_b; p.ln_rows_out = static_cast<bf16 *>(out);
         launch_gemm(p, static_cast<const bf16 *>(A), lda, static_cast<const bf16 *>(W),
                     static_cast<cudaStream_t>(stream));
     })

@@ -22,7 +22,7 @@ EXPORTED = [
     "tc_create_multi", "tc_encode_tile", "tc_encode_tile_rows", "tc_encode_tile_device",
     "tc_plan_rows", "tc_set_stream", "tc_set_profiling", "tc_get_stats", "tc_reset_stats", "tc_host_alloc",
     "tc_host_free",
-    "tcb_op_gemm", "tcb_op_gemm_ln", "tcb_op_gemm_ln_rows", "tcb_op_gemm_ln_noalloc", "tcb_op_count", "tcb_op_gather", "tcb_op_emb1", "tcb_op_attention",
+    "tcb_op_gemm", "tcb_op_gemm_ln", "tcb_op_gemm_ln_noalloc", "tcb_op_count", "tcb_op_gather", "tcb_op_emb1", "tcb_op_attention",
     "tcb_op_layernorm640", "tcb_op_pool", "tcb_op_ln_relu2560", "tcb_op_out128", "tcb_op_wait_probe", "tcb_attention_plan",
 ]
 
@@ -95,8 +95,6 @@ def load_library(path: os.PathLike | None = None) -> C.CDLL:
     lib.tcb_op_gemm.argtypes = [vp, i32, vp, vp, i32, vp, i32, vp, i32, vp, vp, vp, i32, i32, i32, i32, i32, i32, vp, vp]
     lib.tcb_op_gemm_ln.restype = i32
     lib.tcb_op_gemm_ln.argtypes = [vp, i32, vp, vp, vp, i32, vp, vp, vp, i32, i32, i32, vp, vp]
-    lib.tcb_op_gemm_ln_rows.restype = i32
-    lib.tcb_op_gemm_ln_rows.argtypes = [vp, i32, vp, vp, vp, i32, vp, vp, vp, vp, i32, i32, vp, vp]
     lib.tcb_op_gemm_ln_noalloc.restype = i32
     lib.tcb_op_gemm_ln_noalloc.argtypes = [vp, i32, vp, vp, vp, i32, vp, vp, vp, i32, i32, vp]
     lib.tcb_op_count.restype = i32

@@ -383,35 +383,3 @@ def test_gemm_layernorm_fused(lib, M, K):
     # rel 2^-6: one bf16 ulp of the larger of the two values when they straddle a power of two
     check_bf16(out, ref, yf.abs() * rstd * gam.abs() + bet.abs(), rel=2.0 ** -6, acc=2.0 ** -7, atol=1e-4,
                exact_frac=0.9)
-
-
-@pytest.mark.parametrize("M,K", [(1, 640), (129, 640), (300, 2560), (5000, 2560), (70000, 640)])
-def test_gemm_layernorm_rowpass(lib, M, K):
-    """The row-pass LayerNorm inside the GEMM (the default LN1 / LN2 of the
-    back end) is bit-identical to the GEMM followed by the LayerNorm kernel,
-    and within the LayerNorm tolerance of the fp32 reference."""
-    g = torch.Generator(device="cuda").manual_seed(7 * M + K)
-    A = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
-    W = (torch.randn(640, K, device="cuda", generator=g) / K ** 0.5).to(torch.bfloat16)
-    bias = torch.randn(640, device="cuda", generator=g) * 0.1
-    res = torch.randn(M, 640, device="cuda", generator=g).to(torch.bfloat16)
-    gam = 1 + 0.1 * torch.randn(640, device="cuda", generator=g)
-    bet = 0.1 * torch.randn(640, device="cuda", generator=g)
-    y = torch.empty(M, 640, device="cuda", dtype=torch.bfloat16)
-    out = torch.full((M, 640), float("nan"), device="cuda", dtype=torch.bfloat16)
-    status = torch.zeros(1, dtype=torch.int32, device="cuda")
-    assert lib.tcb_op_gemm_ln_rows(_p(A), K, _p(W), _p(bias), _p(res), 640, _p(gam), _p(bet), _p(y), _p(out), M, K,
-                                   _p(status), _stream()) == 0
-    # two-launch path: GEMM into y2, LayerNorm kernel into out2
-    y2 = torch.empty(M, 640, device="cuda", dtype=torch.bfloat16)
-    out2 = torch.empty(M, 640, device="cuda", dtype=torch.bfloat16)
-    assert lib.tcb_op_gemm(_p(A), K, _p(W), _p(bias), 0, _p(res), 640, None, 1, None, None, _p(y2), 640, M, 640, K,
-                           0, 1, _p(status), _stream()) == 0
-    assert lib.tcb_op_layernorm640(_p(y2), M, _p(gam), _p(bet), _p(out2), _stream()) == 0
-    torch.cuda.synchronize()
-    assert status.item() == 0
-    assert torch.equal(out.view(torch.int16), out2.view(torch.int16))
-    yf = y2.float()
-    ref = torch.nn.functional.layer_norm(yf, (640,), gam, bet, 1e-5).to(torch.bfloat16)
-    rstd = 1.0 / torch.sqrt(yf.var(-1, unbiased=False, keepdim=True) + 1e-5)
-    check_bf16(out, ref, yf.abs() * rstd * gam.abs() + bet.abs(), acc=2.0 ** -14)
