@@ -240,7 +240,7 @@ struct Dev {
     ModelDev m;
     int64_t tok_cap = 0, px_cap = 0;
     // chunk workspace
-    DevBuf<float> rec;
+    DevBuf<float> rec, logits;
     DevBuf<bf16> y, x, x1, att, qkv, hbuf, fused, r1, r2;
     DevBuf<int> status;
     // tc_encode inputs / output
@@ -266,7 +266,7 @@ struct Dev {
         if (device >= 0) cudaSetDevice(device);
         if (own) cudaStreamSynchronize(own);
         for (auto e : evpool) cudaEventDestroy(e);
-        rec.release(); y.release(); x.release(); x1.release(); att.release(); qkv.release(); hbuf.release();
+        rec.release(); logits.release(); y.release(); x.release(); x1.release(); att.release(); qkv.release(); hbuf.release();
         fused.release(); r1.release(); r2.release(); status.release(); in2.release(); in1.release(); outf.release();
         tile.release(); n2.release(); n1.release(); bins2.release(); bins1.release(); off2.release(); off1.release();
         list2.release(); list1.release();
@@ -331,6 +331,7 @@ static void dev_init(Dev &d, int device, const Blob &blob, const ModelOff &off) 
     CK(cudaMemset(d.status.p, 0, sizeof(int)));
     const size_t T = (size_t)d.tok_cap, P = (size_t)d.px_cap;
     d.rec.ensure(T * 11);
+    d.logits.ensure(T);
     d.y.ensure(T * D); d.x.ensure(T * D); d.x1.ensure(T * D); d.att.ensure(T * D);
     d.qkv.ensure(T * 3 * D); d.hbuf.ensure(T * FF);
     d.fused.ensure(P * 2 * D); d.r1.ensure(P * RED); d.r2.ensure(P * OUT);
@@ -386,6 +387,7 @@ static void backbone(Dev &d, int b, const float *rec, Segs segs, int64_t M, int 
                      const AttnPlan *plan = nullptr) {
     const BackboneDev &B = d.m.bb[b];
     if (M > d.tok_cap) throw std::runtime_error("chunk larger than the token workspace");
+    bool logits_ready = false;
     if (M > 0) {
         d.mark(TC_CAT_EMB1);
         launch_emb1(B.C, rec, M, B.w1t, B.b1, d.y.p, d.st);
@@ -407,13 +409,17 @@ static void backbone(Dev &d, int b, const float *rec, Segs segs, int64_t M, int 
                 gemm(d, GK_FFN1, B.ffn1[l], d.x1.p, M, d.hbuf.p, true);
                 gemm(d, GK_FFN2, B.ffn2[l], d.hbuf.p, M, d.y.p, false, d.x1.p);
                 d.mark(TC_CAT_LN);
-                launch_layernorm640(d.y.p, M, B.ln2g[l], B.ln2b[l], d.x.p, d.st);
+                // the last LN2 also writes the pooling logits, so pooling reads x once
+                const bool last = l == NL - 1;
+                launch_layernorm640(d.y.p, M, B.ln2g[l], B.ln2b[l], d.x.p, d.st, last ? B.poolq : nullptr, B.poolb,
+                                    last ? d.logits.p : nullptr);
+                logits_ready = last;
                 d.stats.launches += 2;
             }
         }
     }
     d.mark(TC_CAT_POOL);
-    launch_pool(d.x.p, segs, npix, B.poolq, B.poolb, d.fused.p, b * D, d.st);
+    launch_pool(d.x.p, segs, npix, B.poolq, B.poolb, d.fused.p, b * D, d.st, logits_ready ? d.logits.p : nullptr);
     d.stats.launches += 1;
     d.stats.tokens += double(M);
 }

@@ -206,6 +206,19 @@ __device__ __forceinline__ uint64_t umma_desc_sw128_mn(uint32_t smem_addr, uint3
            ((uint64_t)(1024 >> 4) << 32) | ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
 
+// The same two descriptors for tiles written by TMA with 64-byte swizzle: rows
+// of 32 bf16 (64 B), 8-row groups 512 B apart (layout type 4 = SWIZZLE_64B).
+// K-major: +32 bytes along K inside the atom = +2 in the >>4 address field.
+// MN-major: column blocks of 32 MN elements `mn_block_bytes` apart (LBO).
+__device__ __forceinline__ uint64_t umma_desc_sw64(uint32_t smem_addr) {
+    return (uint64_t)((smem_addr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(512 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)4 << 61);
+}
+__device__ __forceinline__ uint64_t umma_desc_sw64_mn(uint32_t smem_addr, uint32_t mn_block_bytes) {
+    return (uint64_t)((smem_addr >> 4) & 0x3FFFu) | ((uint64_t)((mn_block_bytes >> 4) & 0x3FFFu) << 16) |
+           ((uint64_t)(512 >> 4) << 32) | ((uint64_t)1 << 46) | ((uint64_t)4 << 61);
+}
+
 // Instruction descriptor for kind::f16: D f32, A and B bf16, both K-major.
 __host__ __device__ constexpr uint32_t umma_idesc_bf16(int M, int N) {
     return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);

@@ -703,11 +703,298 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     if (warp == 1) tmem_dealloc(tb, 512);
 }
 
+// ------------------------------------------------------------------ attention, 128 < T <= 256 (tcgen05)
+// Persistent, one CTA per SM, over (pixel, head, query half) items: half 0 is
+// the query rows [0, 128), half 1 the rows [128, T); both attend over all T
+// keys. The two halves of a head are adjacent items, so the second read of its
+// K and V rows comes from L2.
+//   warp 0       TMA, boxes of 32 rows x 32 columns with 64-byte swizzle,
+//                five 32-column slabs per matrix covering the head's 160
+//                columns exactly. Lane 0: the item's query rows into the Q
+//                stage and its T key rows into the K stage, both released once
+//                S has read them; lane 1: its T value rows into the V stage,
+//                released once O has read it.
+//   warp 1       TMEM allocation and MMA issue (one thread):
+//                  S = Q K^T   A = Q, B = K (both K-major), M = 128, N = Tpad <= 256, 10 k-steps
+//                  O = P V     A = P from TMEM, B = V (MN-major), M = 128, N = 160, Tpad / 16 k-steps
+//                S of the next item waits until O of this one has read P, which
+//                shares S's columns.
+//   warps 2-17   softmax: four warps per TMEM lane quadrant, one query row per
+//                lane and 64 of the 256 key columns per warp: s = bf16(scale *
+//                S) and the row max, e = exp(s - max) and the row sum, then
+//                P = bf16(e / sum) over the T real keys back into TMEM; the
+//                four partial maxima and sums of a row meet in shared memory.
+//   warps 18-21  O rows -> bf16 -> att, 32 columns at a time through a 2 KB
+//                staging buffer per warp (8 rows x 64 contiguous bytes per store).
+// Tensor memory (512 columns): S / P [0, 256) (P overwrites the first Tpad/2
+// columns of S), O [256, 416).
+// K/V rows past T (up to the next multiple of 32) belong to the next pixel or
+// are zero-filled past the chunk; S columns >= T are masked and P is 0 there.
+// Query rows past the half's last row are never stored.
+// Every mbarrier wait is bounded.
+constexpr int A2_QSLAB = 128 * 64;                 // 128 rows x 32 bf16 = 8 KB
+constexpr int A2_KSLAB = 256 * 64;                 // 256 rows x 32 bf16 = 16 KB
+constexpr int A2_Q_OFF = 0, A2_K_OFF = 5 * A2_QSLAB, A2_V_OFF = A2_K_OFF + 5 * A2_KSLAB;
+constexpr int A2_RED_OFF = A2_V_OFF + 5 * A2_KSLAB;  // partial max and sum: [slice][row] floats
+constexpr int A2_OST_OFF = A2_RED_OFF + AT_RED_BYTES;
+constexpr int A2_BAR_OFF = A2_OST_OFF + 4 * AT_OSTAGE;
+constexpr int A2_SMEM = 1024 + A2_BAR_OFF + 256;
+constexpr uint32_t A2_SCOL = 0, A2_OCOL = 256;
+static_assert(A2_SMEM <= 227 * 1024, "k_attention_tc256 shared memory");
+
+__global__ void __launch_bounds__(AT_THREADS, 1)
+    k_attention_tc256(const __grid_constant__ CUtensorMap tm, Segs segs, int64_t nitems, bf16 *__restrict__ att,
+                      float scale, int *status) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    float *red_max = reinterpret_cast<float *>(smem + A2_RED_OFF), *red_sum = red_max + 4 * 128;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + A2_BAR_OFF);
+    uint64_t *qk_full = bars, *qk_empty = bars + 1, *v_full = bars + 2, *v_empty = bars + 3;
+    uint64_t *s_full = bars + 4, *p_full = bars + 5, *o_full = bars + 6, *o_free = bars + 7, *pv_done = bars + 8;
+    uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 9);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        mbar_init(qk_full, 1);
+        mbar_init(qk_empty, 1);
+        mbar_init(v_full, 1);
+        mbar_init(v_empty, 1);
+        mbar_init(s_full, 1);
+        mbar_init(p_full, AT_SOFT_WARPS);
+        mbar_init(o_full, 1);
+        mbar_init(o_free, 4);
+        mbar_init(pv_done, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+        prefetch_tensormap(&tm);
+    }
+    if (warp == 1) { tmem_alloc(tmem_holder, 512); tmem_relinquish(); }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tb = *tmem_holder;
+    // Item it: launch segment it >> 3, head (it >> 1) & 3, query half it & 1.
+    // Every role walks the items with 128 < T <= 256 in the same order; any
+    // other length is skipped by all roles (a longer one is reported).
+    auto item_at = [&](int64_t it, int64_t &t0, int &T, int &h, int &half) {
+        const int64_t p = seg_pix(segs, it >> 3);
+        h = (int)((it >> 1) & 3);
+        half = (int)(it & 1);
+        t0 = seg_at(segs, p);
+        const int64_t len = seg_at(segs, p + 1) - t0;
+        T = (len > 128 && len <= 256) ? (int)len : 0;
+        if (len > 256 && warp == 0 && lane == 0 && status) atomicCAS(status, 0, ERR_BAD_SEGMENT);
+    };
+    auto next_item = [&](int64_t it, int64_t &t0, int &T, int &h, int &half) -> int64_t {
+        for (; it < nitems; it += gridDim.x) {
+            item_at(it, t0, T, h, half);
+            if (T > 0) break;
+        }
+        return it;
+    };
+
+    if (warp == 0) {
+        if (lane < 2) {  // lane 0 loads Q and K, lane 1 loads V
+            int j = 0;
+            int64_t t0;
+            int T, h, half;
+            for (int64_t it = next_item(blockIdx.x, t0, T, h, half); it < nitems;
+                 it = next_item(it + gridDim.x, t0, T, h, half)) {
+                const int nbk = (T + 31) >> 5;
+                if (lane == 0) {
+                    const int Tq = half ? T - 128 : 128, nbq = (Tq + 31) >> 5;
+                    const int q0 = (int)t0 + half * 128;
+                    if (!mbar_wait(qk_empty, (j & 1) ^ 1, abort_flag, status, ERR_WAIT_SMEM_EMPTY)) break;
+                    mbar_arrive_expect_tx(qk_full, (uint32_t)((nbq + nbk) * 5 * 32 * 64));
+                    for (int rb = 0; rb < nbq; ++rb)
+                        for (int sl = 0; sl < 5; ++sl)
+                            tma_load_2d(smem + A2_Q_OFF + sl * A2_QSLAB + rb * 2048, &tm, h * HD + sl * 32, q0 + rb * 32,
+                                        qk_full);
+                    for (int rb = 0; rb < nbk; ++rb)
+                        for (int sl = 0; sl < 5; ++sl)
+                            tma_load_2d(smem + A2_K_OFF + sl * A2_KSLAB + rb * 2048, &tm, D + h * HD + sl * 32,
+                                        (int)t0 + rb * 32, qk_full);
+                } else {
+                    if (!mbar_wait(v_empty, (j & 1) ^ 1, abort_flag, status, ERR_WAIT_SMEM_EMPTY)) break;
+                    mbar_arrive_expect_tx(v_full, (uint32_t)(nbk * 5 * 32 * 64));
+                    for (int rb = 0; rb < nbk; ++rb)
+                        for (int sl = 0; sl < 5; ++sl)
+                            tma_load_2d(smem + A2_V_OFF + sl * A2_KSLAB + rb * 2048, &tm, 2 * D + h * HD + sl * 32,
+                                        (int)t0 + rb * 32, v_full);
+                }
+                ++j;
+            }
+            // every stage released: no MMA still reads shared memory at exit
+            mbar_wait(lane == 0 ? qk_empty : v_empty, (j & 1) ^ 1, abort_flag, status, ERR_WAIT_SMEM_EMPTY);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc_o = umma_idesc_bf16_bmn(128, HD);
+            const uint32_t sq = smem_u32(smem + A2_Q_OFF), sk = smem_u32(smem + A2_K_OFF),
+                           sv = smem_u32(smem + A2_V_OFF);
+            int j = 0;
+            int64_t t0;
+            int T, h, half;
+            for (int64_t it = next_item(blockIdx.x, t0, T, h, half); it < nitems;
+                 it = next_item(it + gridDim.x, t0, T, h, half)) {
+                const int tpad = (T + 15) & ~15;
+                // S(j): its columns hold P(j - 1) until O(j - 1) has read it
+                if (!mbar_wait(qk_full, j & 1, abort_flag, status, ERR_WAIT_TMA_FULL)) break;
+                if (j > 0 && !mbar_wait(pv_done, (j - 1) & 1, abort_flag, status, ERR_WAIT_TMEM_EMPTY)) break;
+                tc_fence_after();
+                const uint32_t idesc_s = umma_idesc_bf16(128, tpad);
+#pragma unroll
+                for (int k = 0; k < HD / 16; ++k) {
+                    const uint32_t sl = (uint32_t)(k >> 1);
+                    umma_bf16(tb + A2_SCOL, umma_desc_sw64(sq + sl * A2_QSLAB) + (uint64_t)(2 * (k & 1)),
+                              umma_desc_sw64(sk + sl * A2_KSLAB) + (uint64_t)(2 * (k & 1)), idesc_s, k > 0);
+                }
+                umma_commit(s_full);
+                umma_commit(qk_empty);
+                // O(j) = P(j) V(j)
+                if (!mbar_wait(v_full, j & 1, abort_flag, status, ERR_WAIT_TMA_FULL)) break;
+                if (!mbar_wait(p_full, j & 1, abort_flag, status, ERR_WAIT_TMEM_FULL)) break;
+                if (!mbar_wait(o_free, (j & 1) ^ 1, abort_flag, status, ERR_WAIT_TMEM_EMPTY)) break;
+                tc_fence_after();
+                for (int k = 0; k < tpad / 16; ++k)
+                    umma_bf16_tmem_a(tb + A2_OCOL, tb + A2_SCOL + (uint32_t)(k * 8),
+                                     umma_desc_sw64_mn(sv + (uint32_t)(k * 16 * 64), A2_KSLAB), idesc_o, k > 0);
+                umma_commit(o_full);
+                umma_commit(v_empty);
+                umma_commit(pv_done);
+                ++j;
+            }
+            // the last item's arrivals have landed before the CTA's shared memory is released
+            if (j > 0) mbar_wait(pv_done, (j - 1) & 1, abort_flag, status, ERR_WAIT_TMEM_EMPTY);
+        }
+    } else if (warp < AT_IO_WARP0) {
+        // softmax: quadrant = warp % 4 (the TMEM lanes this warp may access), 64-column slice
+        const int quad = warp & 3, slice = (warp - 2) >> 2, r = quad * 32 + lane, c0 = slice * 64;
+        const uint32_t lanebits = (uint32_t)(quad * 32) << 16;
+        int j = 0;
+        int64_t t0;
+        int T, h, half;
+        for (int64_t it = next_item(blockIdx.x, t0, T, h, half); it < nitems;
+             it = next_item(it + gridDim.x, t0, T, h, half)) {
+            const int tpad = (T + 15) & ~15;
+            if (!mbar_wait(s_full, j & 1, abort_flag, status, ERR_WAIT_TMEM_FULL)) break;
+            tc_fence_after();
+            uint32_t v[4][16];  // 64 columns of the S row, then s, then e, as f32 bits
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+                if (c0 + q * 16 < tpad) tmem_ld16(tb + lanebits + A2_SCOL + (uint32_t)(c0 + q * 16), v[q]);
+            tmem_ld_wait();
+            float mx = -INFINITY;
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+                if (c0 + q * 16 < tpad) {
+#pragma unroll
+                    for (int k = 0; k < 16; ++k) {
+                        const int col = c0 + q * 16 + k;
+                        const float x = col < T ? bf16_round(__uint_as_float(v[q][k]) * scale) : -INFINITY;
+                        v[q][k] = __float_as_uint(x);
+                        mx = fmaxf(mx, x);
+                    }
+                }
+            red_max[slice * 128 + r] = mx;
+            named_bar_sync(1 + quad, 128);
+            mx = fmaxf(fmaxf(red_max[r], red_max[128 + r]), fmaxf(red_max[256 + r], red_max[384 + r]));
+            float z = 0.f;
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+                if (c0 + q * 16 < tpad) {
+#pragma unroll
+                    for (int k = 0; k < 16; ++k) {
+                        const float ex = expf(__uint_as_float(v[q][k]) - mx);  // 0 for masked columns
+                        v[q][k] = __float_as_uint(ex);
+                        z += ex;
+                    }
+                }
+            red_sum[slice * 128 + r] = z;
+            named_bar_sync(1 + quad, 128);
+            z = ((red_sum[r] + red_sum[128 + r]) + red_sum[256 + r]) + red_sum[384 + r];
+            const float inv = 1.f / z;
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+                if (c0 + q * 16 < tpad) {
+                    uint32_t w[8];
+#pragma unroll
+                    for (int k = 0; k < 8; ++k)
+                        w[k] = pack_bf16x2(__uint_as_float(v[q][2 * k]) * inv, __uint_as_float(v[q][2 * k + 1]) * inv);
+                    tmem_st8(tb + lanebits + A2_SCOL + (uint32_t)(c0 / 2 + q * 8), w);
+                }
+            tmem_st_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(p_full);
+            ++j;
+        }
+    } else {
+        // O warps: each drains its TMEM lane quadrant (32 query rows) of O(j)
+        const int quad = warp & 3;
+        const uint32_t lanebits = (uint32_t)(quad * 32) << 16;
+        uint8_t *stage = smem + A2_OST_OFF + (warp - AT_IO_WARP0) * AT_OSTAGE;
+        uint4 *my_row = reinterpret_cast<uint4 *>(stage + lane * 64);
+        const int sw = (lane >> 1) & 3;
+        int j = 0;
+        int64_t t0;
+        int T, h, half;
+        for (int64_t it = next_item(blockIdx.x, t0, T, h, half); it < nitems;
+             it = next_item(it + gridDim.x, t0, T, h, half)) {
+            if (!mbar_wait(o_full, j & 1, abort_flag, status, ERR_WAIT_TMEM_FULL)) break;
+            tc_fence_after();
+            const int Tq = half ? T - 128 : 128;
+            const int nrows = Tq - quad * 32;  // real rows of this quadrant (uniform per warp)
+            if (nrows > 0) {
+                bf16 *dst = att + (t0 + half * 128 + quad * 32) * D + h * HD;
+#pragma unroll 1
+                for (int c = 0; c < HD / 32; ++c) {
+                    uint32_t v[16], w[16];
+                    tmem_ld16(tb + lanebits + A2_OCOL + (uint32_t)(c * 32), v);
+                    tmem_ld16(tb + lanebits + A2_OCOL + (uint32_t)(c * 32 + 16), w);
+                    tmem_ld_wait();
+                    uint32_t o[16];
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) {
+                        o[k] = pack_bf16x2(__uint_as_float(v[2 * k]), __uint_as_float(v[2 * k + 1]));
+                        o[8 + k] = pack_bf16x2(__uint_as_float(w[2 * k]), __uint_as_float(w[2 * k + 1]));
+                    }
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) my_row[k ^ sw] = make_uint4(o[4 * k], o[4 * k + 1], o[4 * k + 2], o[4 * k + 3]);
+                    __syncwarp();
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const int rr = i * 8 + (lane >> 2), k = lane & 3;
+                        const uint4 val = reinterpret_cast<const uint4 *>(stage + rr * 64)[k ^ ((rr >> 1) & 3)];
+                        if (rr < nrows) *reinterpret_cast<uint4 *>(dst + (int64_t)rr * D + c * 32 + k * 8) = val;
+                    }
+                    __syncwarp();
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(o_free);
+            ++j;
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc(tb, 512);
+}
+
 // ------------------------------------------------------------------ LayerNorm
 // Warp per row of 640, two-pass f32 statistics.
 
+// With pool_q set (the last layer's LN2), each row's attention-pooling logit
+// s = sum_k y[k] q[k] + qb of the bf16 output row is also written to
+// logits[row], summed in exactly the order k_pool sums it (per lane over its
+// five 4-column groups, then the warp), so the pooling kernel reads x once.
 __global__ void __launch_bounds__(256) k_layernorm640(const bf16 *__restrict__ x, int64_t M, const float *__restrict__ g,
-                                                      const float *__restrict__ b, bf16 *__restrict__ y) {
+                                                      const float *__restrict__ b, bf16 *__restrict__ y,
+                                                      const float *__restrict__ pool_q, float pool_qb,
+                                                      float *__restrict__ logits) {
     // Grid-stride over rows, one warp per row: lane l holds columns
     // 128j + 4l .. 128j + 4l + 3 (j = 0..4) packed as bf16, so each 8-byte
     // load instruction of the warp reads 256 contiguous bytes. The next row is
@@ -748,6 +1035,7 @@ __global__ void __launch_bounds__(256) k_layernorm640(const bf16 *__restrict__ x
         }
         const float rstd = 1.f / sqrtf(warp_sum(ss) / (float)D + LN_EPS);
         bf16 *yr = y + r * D + lane * 4;
+        float dq = 0.f;
 #pragma unroll
         for (int j = 0; j < 5; ++j) {
             const int c = j * 128 + lane * 4;
@@ -757,6 +1045,13 @@ __global__ void __launch_bounds__(256) k_layernorm640(const bf16 *__restrict__ x
             const uint32_t o1 = pack_bf16x2((bf16lo(q[j].y) - mean) * rstd * gg.z + bb.z,
                                             (bf16hi(q[j].y) - mean) * rstd * gg.w + bb.w);
             *reinterpret_cast<uint2 *>(yr + j * 128) = make_uint2(o0, o1);
+            if (pool_q)
+                dq += bf16lo(o0) * pool_q[c] + bf16hi(o0) * pool_q[c + 1] + bf16lo(o1) * pool_q[c + 2] +
+                      bf16hi(o1) * pool_q[c + 3];
+        }
+        if (pool_q) {
+            dq = warp_sum(dq);
+            if (lane == 0) logits[r] = dq + pool_qb;
         }
 #pragma unroll
         for (int j = 0; j < 5; ++j) q[j] = qn[j];
@@ -765,9 +1060,11 @@ __global__ void __launch_bounds__(256) k_layernorm640(const bf16 *__restrict__ x
 
 // ------------------------------------------------------------------ pooling
 // One CTA (160 threads) per pixel: warp-per-step logits, softmax in warp 0,
-// then each thread accumulates 4 columns over the steps.
+// then each thread accumulates 4 columns over the steps. When the last
+// LayerNorm already wrote the logits (logits != null), x is read once.
 __global__ void __launch_bounds__(160) k_pool(const bf16 *__restrict__ x, Segs segs, const float *__restrict__ q,
-                                              float qb, bf16 *__restrict__ fused, int col0) {
+                                              float qb, bf16 *__restrict__ fused, int col0,
+                                              const float *__restrict__ logits) {
     __shared__ float w[256];
     const int64_t i = blockIdx.x;
     const int64_t t0 = seg_at(segs, i);
@@ -779,7 +1076,9 @@ __global__ void __launch_bounds__(160) k_pool(const bf16 *__restrict__ x, Segs s
         return;
     }
     const bf16 *xp = x + t0 * D;
-    for (int t = warp; t < T; t += 5) {
+    if (logits) {
+        for (int t = threadIdx.x; t < T; t += blockDim.x) w[t] = logits[t0 + t];
+    } else for (int t = warp; t < T; t += 5) {
         float d = 0.f;
 #pragma unroll
         for (int j = 0; j < 5; ++j) {
@@ -963,9 +1262,9 @@ template <int NT> static void attention_nt(const bf16 *qkv, Segs segs, int64_t n
     k_attention<NT><<<grid, 32 * warps, smem, st>>>(qkv, segs, att, 1.f / std::sqrt((float)HD));
 }
 
-// TC_ATTN_TC: 0 = always the mma.sync kernel, 1 (default) = the tcgen05 kernel
-// for a series longer than AT_MMA_MAX_T and up to 128 steps, 2 = the tcgen05
-// kernel whenever T <= 128.
+// TC_ATTN_TC: 0 = always the mma.sync kernel; 1 (default) = the tcgen05 kernels
+// for a series longer than AT_MMA_MAX_T (k_attention_tc up to 128 steps,
+// k_attention_tc256 above); 2 = the tcgen05 kernels for every length.
 static int attention_tcgen05() {
     static const int mode = [] {
         const char *e = std::getenv("TC_ATTN_TC");
@@ -1001,6 +1300,26 @@ static void attention_tc(const bf16 *qkv, Segs segs, int64_t npix, int64_t ntok,
     k_attention_tc<<<grid, AT_THREADS, AT_SMEM, st>>>(tm, segs, items, att, 1.f / std::sqrt((float)HD), status);
 }
 
+static void attention_tc256(const bf16 *qkv, Segs segs, int64_t npix, int64_t ntok, bf16 *att, int *status,
+                            cudaStream_t st) {
+    static int grid_per_dev[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!grid_per_dev[dev & 63]) {
+        cudaError_t e = cudaFuncSetAttribute(k_attention_tc256, cudaFuncAttributeMaxDynamicSharedMemorySize, A2_SMEM);
+        if (e != cudaSuccess) throw std::runtime_error(std::string("attention smem attribute: ") + cudaGetErrorString(e));
+        int sms = 0;
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        grid_per_dev[dev & 63] = std::max(1, sms);
+    }
+    // qkv rows [0, ntok) x 1920 columns; boxes of 32 rows x 32 columns, 64-byte swizzle
+    CUtensorMap tm;
+    make_tmap_box(&tm, qkv, (uint64_t)ntok, (uint64_t)(3 * D), (uint64_t)(3 * D), 32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
+    const int64_t items = npix * NH * 2;
+    const unsigned grid = (unsigned)std::min<int64_t>(items, grid_per_dev[dev & 63]);
+    k_attention_tc256<<<grid, AT_THREADS, A2_SMEM, st>>>(tm, segs, items, att, 1.f / std::sqrt((float)HD), status);
+}
+
 int attention_class(int T) {
     if (T > 128) return 2;
     const int mode = attention_tcgen05();
@@ -1031,6 +1350,8 @@ static void attention_of_class(int cls, const bf16 *qkv, Segs segs, int64_t npix
     const int Tpad = (tmax + 15) & ~15;
     if (cls == 1) {
         attention_tc(qkv, segs, npix, ntok, att, status, st);
+    } else if (cls == 2 && attention_tcgen05() != 0) {
+        attention_tc256(qkv, segs, npix, ntok, att, status, st);
     } else {
         if (Tpad <= 32) attention_nt<4>(qkv, segs, npix, Tpad, att, st);
         else if (Tpad <= 64) attention_nt<8>(qkv, segs, npix, Tpad, att, st);
@@ -1066,7 +1387,8 @@ int launch_attention(const bf16 *qkv, Segs segs, int64_t npix, int64_t ntok, int
     return 1;
 }
 
-void launch_layernorm640(const bf16 *x, int64_t M, const float *g, const float *b, bf16 *y, cudaStream_t st) {
+void launch_layernorm640(const bf16 *x, int64_t M, const float *g, const float *b, bf16 *y, cudaStream_t st,
+                         const float *pool_q, float pool_qb, float *logits) {
     if (M <= 0) return;
     // grid-stride: as many blocks as fit on the device at once
     static int resident[64] = {};
@@ -1079,14 +1401,14 @@ void launch_layernorm640(const bf16 *x, int64_t M, const float *g, const float *
         resident[dev & 63] = std::max(1, per_sm) * std::max(1, sms);
     }
     const unsigned grid = (unsigned)std::min<int64_t>(blocks_for(M, 8), resident[dev & 63]);
-    k_layernorm640<<<grid, 256, 0, st>>>(x, M, g, b, y);
+    k_layernorm640<<<grid, 256, 0, st>>>(x, M, g, b, y, pool_q, pool_qb, logits);
     check_launch("k_layernorm640");
 }
 
 void launch_pool(const bf16 *x, Segs segs, int64_t npix, const float *q, float qb, bf16 *fused, int col0,
-                 cudaStream_t st) {
+                 cudaStream_t st, const float *logits) {
     if (npix <= 0) return;
-    k_pool<<<(unsigned)npix, 160, 0, st>>>(x, segs, q, qb, fused, col0);
+    k_pool<<<(unsigned)npix, 160, 0, st>>>(x, segs, q, qb, fused, col0, logits);
     check_launch("k_pool");
 }
 

@@ -56,7 +56,9 @@ void launch_emb1(int C, const float *rec, int64_t M, const float *w1t, const flo
 //   class 0: the mma.sync kernel, for T <= 48 (every T <= 128 with TC_ATTN_TC=0);
 //   class 1: the tcgen05 kernel, for 48 < T <= 128 (every T <= 128 with
 //            TC_ATTN_TC=2); its bounded waits report into *status (may be null);
-//   class 2: the mma.sync kernel, for T > 128.
+//   class 2: the tcgen05 kernel for 128 < T <= 256 (query halves of 128 rows,
+//            S over up to 256 keys in TMEM), or the mma.sync kernel with
+//            TC_ATTN_TC=0; its bounded waits report into *status.
 int attention_class(int T);
 
 // A chunk's pixels with T > 0 listed class by class (device memory), with the
@@ -79,12 +81,17 @@ int launch_attention(const __nv_bfloat16 *qkv, Segs segs, int64_t npix, int64_t 
                      int *status, cudaStream_t st);
 
 // y = bf16(LN(x) * g + b) over rows of 640 (g, b may be null for no affine).
+// With pool_q set, also logits[row] = y_row . pool_q + pool_qb in f32, in the
+// summation order of the pooling kernel (the last layer's LN2 feeds pooling).
 void launch_layernorm640(const __nv_bfloat16 *x, int64_t M, const float *g, const float *b, __nv_bfloat16 *y,
-                         cudaStream_t st);
+                         cudaStream_t st, const float *pool_q = nullptr, float pool_qb = 0.f,
+                         float *logits = nullptr);
 
 // fused[i, col0:col0+640] = bf16(sum_t softmax_t(x_t . q + qb) x_t) (tessera_cpu.cpp:434-455).
+// logits: the per-token logits x_t . q + qb from launch_layernorm640, or null
+// to compute them here (a second read of x).
 void launch_pool(const __nv_bfloat16 *x, Segs segs, int64_t npix, const float *q, float qb, __nv_bfloat16 *fused,
-                 int col0, cudaStream_t st);
+                 int col0, cudaStream_t st, const float *logits = nullptr);
 
 // r = relu(bf16(LN2560(r) * g + b)) in place (tessera_cpu.cpp:568-571).
 void launch_ln_relu2560(__nv_bfloat16 *r, int64_t P, const float *g, const float *b, cudaStream_t st);
