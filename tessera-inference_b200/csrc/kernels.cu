@@ -329,8 +329,8 @@ __global__ void __launch_bounds__(NTMAX == 24 ? 512 : 256, NTMAX <= 16 ? 2 : 1)
 #pragma unroll
         for (int nt = 0; nt < NTMAX; ++nt)
             if (nt < nnt) {
-                z0 += expf(bf16lo(sp[nt][0]) - mx0) + expf(bf16hi(sp[nt][0]) - mx0);
-                z1 += expf(bf16lo(sp[nt][1]) - mx1) + expf(bf16hi(sp[nt][1]) - mx1);
+                z0 += __expf(bf16lo(sp[nt][0]) - mx0) + __expf(bf16hi(sp[nt][0]) - mx0);
+                z1 += __expf(bf16lo(sp[nt][1]) - mx1) + __expf(bf16hi(sp[nt][1]) - mx1);
             }
 #pragma unroll
         for (int o = 1; o <= 2; o <<= 1) {
@@ -341,8 +341,8 @@ __global__ void __launch_bounds__(NTMAX == 24 ? 512 : 256, NTMAX <= 16 ? 2 : 1)
 #pragma unroll
         for (int nt = 0; nt < NTMAX; ++nt)
             if (nt < nnt) {
-                sp[nt][0] = pack_bf16x2(expf(bf16lo(sp[nt][0]) - mx0) * inv0, expf(bf16hi(sp[nt][0]) - mx0) * inv0);
-                sp[nt][1] = pack_bf16x2(expf(bf16lo(sp[nt][1]) - mx1) * inv1, expf(bf16hi(sp[nt][1]) - mx1) * inv1);
+                sp[nt][0] = pack_bf16x2(__expf(bf16lo(sp[nt][0]) - mx0) * inv0, __expf(bf16hi(sp[nt][0]) - mx0) * inv0);
+                sp[nt][1] = pack_bf16x2(__expf(bf16lo(sp[nt][1]) - mx1) * inv1, __expf(bf16hi(sp[nt][1]) - mx1) * inv1);
             }
         // O = P V, in two halves of 80 columns
         uint32_t *dst0 = r0 < T ? reinterpret_cast<uint32_t *>(att + (t0 + r0) * D + h * HD) : nullptr;
@@ -620,7 +620,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
                 if (c0 + q * 16 < tpad) {
 #pragma unroll
                     for (int k = 0; k < 16; ++k) {
-                        const float ex = expf(__uint_as_float(v[q][k]) - mx);  // 0 for masked columns
+                        const float ex = __expf(__uint_as_float(v[q][k]) - mx);  // 0 for masked columns
                         v[q][k] = __float_as_uint(ex);
                         z += ex;
                     }
@@ -906,7 +906,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
                 if (c0 + q * 16 < tpad) {
 #pragma unroll
                     for (int k = 0; k < 16; ++k) {
-                        const float ex = expf(__uint_as_float(v[q][k]) - mx);  // 0 for masked columns
+                        const float ex = __expf(__uint_as_float(v[q][k]) - mx);  // 0 for masked columns
                         v[q][k] = __float_as_uint(ex);
                         z += ex;
                     }
@@ -991,6 +991,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
 // s = sum_k y[k] q[k] + qb of the bf16 output row is also written to
 // logits[row], summed in exactly the order k_pool sums it (per lane over its
 // five 4-column groups, then the warp), so the pooling kernel reads x once.
+template <bool LOGITS>
 __global__ void __launch_bounds__(256) k_layernorm640(const bf16 *__restrict__ x, int64_t M, const float *__restrict__ g,
                                                       const float *__restrict__ b, bf16 *__restrict__ y,
                                                       const float *__restrict__ pool_q, float pool_qb,
@@ -1001,10 +1002,11 @@ __global__ void __launch_bounds__(256) k_layernorm640(const bf16 *__restrict__ x
     // loaded before the current one is reduced, which keeps two rows (2.5 KB)
     // of loads in flight per warp at a low register count. gamma/beta are read
     // once per block into shared memory.
-    __shared__ __align__(16) float gs[D], bs[D];
+    __shared__ __align__(16) float gs[D], bs[D], qs[LOGITS ? D : 4];
     for (int i = threadIdx.x; i < D; i += blockDim.x) {
         gs[i] = g ? g[i] : 1.f;
         bs[i] = b ? b[i] : 0.f;
+        if constexpr (LOGITS) qs[i] = pool_q[i];
     }
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -1045,11 +1047,10 @@ __global__ void __launch_bounds__(256) k_layernorm640(const bf16 *__restrict__ x
             const uint32_t o1 = pack_bf16x2((bf16lo(q[j].y) - mean) * rstd * gg.z + bb.z,
                                             (bf16hi(q[j].y) - mean) * rstd * gg.w + bb.w);
             *reinterpret_cast<uint2 *>(yr + j * 128) = make_uint2(o0, o1);
-            if (pool_q)
-                dq += bf16lo(o0) * pool_q[c] + bf16hi(o0) * pool_q[c + 1] + bf16lo(o1) * pool_q[c + 2] +
-                      bf16hi(o1) * pool_q[c + 3];
+            if constexpr (LOGITS)
+                dq += bf16lo(o0) * qs[c] + bf16hi(o0) * qs[c + 1] + bf16lo(o1) * qs[c + 2] + bf16hi(o1) * qs[c + 3];
         }
-        if (pool_q) {
+        if constexpr (LOGITS) {
             dq = warp_sum(dq);
             if (lane == 0) logits[r] = dq + pool_qb;
         }
@@ -1396,12 +1397,13 @@ void launch_layernorm640(const bf16 *x, int64_t M, const float *g, const float *
     cudaGetDevice(&dev);
     if (!resident[dev & 63]) {
         int per_sm = 0, sms = 0;
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_layernorm640, 256, 0);
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_layernorm640<false>, 256, 0);
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
         resident[dev & 63] = std::max(1, per_sm) * std::max(1, sms);
     }
     const unsigned grid = (unsigned)std::min<int64_t>(blocks_for(M, 8), resident[dev & 63]);
-    k_layernorm640<<<grid, 256, 0, st>>>(x, M, g, b, y, pool_q, pool_qb, logits);
+    if (pool_q) k_layernorm640<true><<<grid, 256, 0, st>>>(x, M, g, b, y, pool_q, pool_qb, logits);
+    else k_layernorm640<false><<<grid, 256, 0, st>>>(x, M, g, b, y, nullptr, 0.f, nullptr);
     check_launch("k_layernorm640");
 }
 
