@@ -394,7 +394,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 // barrier, issues the MMAs, and signals each CTA's "empty" and "tile full"
 // barriers with one commit per CTA. Each CTA's epilogue drains its own TMEM
 // (its 128 rows) and arrives on the leader's "tile empty" barrier.
-// No load uses cluster multicast.
+// Each CTA loads only into its own shared memory (no load is shared across the pair).
 template <int BN> struct Gemm2Cfg {
     static constexpr int BNH = BN / 2;
     static constexpr int A_BYTES = BM * BK * 2;

@@ -1,42 +1,122 @@
-// .tcw reader with shape validation for the v2 Large pixel student.
+// .tcw reader with shape validation for the v2 Large pixel student. The file
+// is mapped read-only and parsed with a bounds-checked cursor; every error
+// names the tensor and the byte offset it concerns.
 #include "tcw.h"
 
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include <cerrno>
 #include <cstdio>
 #include <cstring>
-#include <memory>
 #include <stdexcept>
 
 namespace tcb {
 
+namespace {
+
+// Read-only mapping of a whole file, unmapped on scope exit.
+class MappedFile {
+  public:
+    explicit MappedFile(const char *path) {
+        const int fd = ::open(path, O_RDONLY | O_CLOEXEC);
+        if (fd < 0) throw std::runtime_error(std::string("cannot open ") + path + ": " + std::strerror(errno));
+        struct stat st;
+        if (::fstat(fd, &st) != 0) {
+            ::close(fd);
+            throw std::runtime_error(std::string("cannot stat ") + path);
+        }
+        size_ = (size_t)st.st_size;
+        if (size_ > 0) {
+            void *m = ::mmap(nullptr, size_, PROT_READ, MAP_PRIVATE, fd, 0);
+            if (m == MAP_FAILED) {
+                ::close(fd);
+                throw std::runtime_error(std::string("cannot map ") + path);
+            }
+            base_ = static_cast<const uint8_t *>(m);
+            ::madvise(const_cast<uint8_t *>(base_), size_, MADV_SEQUENTIAL);
+        }
+        ::close(fd);
+    }
+    ~MappedFile() {
+        if (base_) ::munmap(const_cast<uint8_t *>(base_), size_);
+    }
+    MappedFile(const MappedFile &) = delete;
+    MappedFile &operator=(const MappedFile &) = delete;
+    const uint8_t *data() const { return base_; }
+    size_t size() const { return size_; }
+
+  private:
+    const uint8_t *base_ = nullptr;
+    size_t size_ = 0;
+};
+
+// Bounds-checked little-endian reader over the mapped bytes; every failure
+// names the byte offset and what was being read.
+class Cursor {
+  public:
+    Cursor(const uint8_t *p, size_t n) : p_(p), n_(n) {}
+    size_t left() const { return n_ - at_; }
+    const uint8_t *take(size_t bytes, const std::string &what) {
+        if (bytes > left())
+            throw std::runtime_error("weight file ends at byte " + std::to_string(n_) + " while reading " + what +
+                                     " (" + std::to_string(bytes) + " bytes at offset " + std::to_string(at_) + ")");
+        const uint8_t *q = p_ + at_;
+        at_ += bytes;
+        return q;
+    }
+    template <class T> T scalar(const std::string &what) {
+        T v;
+        std::memcpy(&v, take(sizeof(T), what), sizeof(T));
+        return v;
+    }
+
+  private:
+    const uint8_t *p_;
+    size_t n_, at_ = 0;
+};
+
+constexpr uint32_t MAX_TENSORS = 100000, MAX_NAME = 4096, MAX_RANK = 8;
+constexpr int64_t MAX_ELEMS = int64_t(1) << 32;
+
+}  // namespace
+
 WeightMap load_tcw(const char *path) {
     if (!path) throw std::runtime_error("null weights path");
-    std::unique_ptr<FILE, int (*)(FILE *)> f(std::fopen(path, "rb"), std::fclose);
-    if (!f) throw std::runtime_error(std::string("cannot open ") + path);
-    char magic[4];
-    uint32_t n = 0;
-    if (std::fread(magic, 1, 4, f.get()) != 4 || std::memcmp(magic, "TCW1", 4) || std::fread(&n, 4, 1, f.get()) != 1)
-        throw std::runtime_error("bad weights file");
-    if (n > 100000) throw std::runtime_error("bad weights file: implausible tensor count");
+    const MappedFile file(path);
+    Cursor c(file.data(), file.size());
+    if (file.size() < 8 || std::memcmp(c.take(4, "the magic"), "TCW1", 4) != 0)
+        throw std::runtime_error(std::string(path) + " is not a .tcw weight file (no TCW1 magic)");
+    const uint32_t count = c.scalar<uint32_t>("the tensor count");
+    if (count > MAX_TENSORS) throw std::runtime_error("implausible tensor count " + std::to_string(count));
     WeightMap w;
-    for (uint32_t i = 0; i < n; ++i) {
-        uint32_t len = 0, nd = 0;
-        if (std::fread(&len, 4, 1, f.get()) != 1 || len > 4096) throw std::runtime_error("truncated weights");
-        std::string name(len, '\0');
-        if (std::fread(name.data(), 1, len, f.get()) != len || std::fread(&nd, 4, 1, f.get()) != 1 || nd > 8)
-            throw std::runtime_error("truncated weights");
+    for (uint32_t i = 0; i < count; ++i) {
+        const std::string which = "tensor " + std::to_string(i);
+        const uint32_t name_len = c.scalar<uint32_t>(which + "'s name length");
+        if (name_len > MAX_NAME) throw std::runtime_error(which + ": implausible name length");
+        const uint8_t *name_bytes = c.take(name_len, which + "'s name");
+        std::string name(reinterpret_cast<const char *>(name_bytes), name_len);
+        const uint32_t rank = c.scalar<uint32_t>(name + "'s rank");
+        if (rank > MAX_RANK) throw std::runtime_error(name + ": implausible rank " + std::to_string(rank));
         HostTensor t;
-        t.shape.resize(nd);
-        if (std::fread(t.shape.data(), 8, nd, f.get()) != nd) throw std::runtime_error("truncated weights");
-        int64_t count = 1;
-        for (auto s : t.shape) {
-            if (s < 0 || s > (int64_t(1) << 32)) throw std::runtime_error("bad weights file: dimension of " + name);
-            count *= s;
+        t.shape.resize(rank);
+        int64_t elems = 1;
+        for (uint32_t d = 0; d < rank; ++d) {
+            t.shape[d] = c.scalar<int64_t>(name + "'s dimensions");
+            if (t.shape[d] < 0 || t.shape[d] > MAX_ELEMS) throw std::runtime_error(name + ": dimension out of range");
+            elems *= t.shape[d];
+            if (elems > MAX_ELEMS) throw std::runtime_error(name + ": tensor too large");
         }
-        if (count > (int64_t(1) << 32)) throw std::runtime_error("bad weights file: tensor too large: " + name);
-        t.data.resize(count);
-        if (std::fread(t.data.data(), 4, count, f.get()) != size_t(count)) throw std::runtime_error("truncated weights");
-        w.emplace(std::move(name), std::move(t));
+        const uint8_t *values = c.take((size_t)elems * sizeof(float), name + "'s values");
+        t.data.resize((size_t)elems);
+        std::memcpy(t.data.data(), values, (size_t)elems * sizeof(float));
+        if (!w.emplace(std::move(name), std::move(t)).second)
+            throw std::runtime_error(which + ": a tensor of that name was already read");
     }
+    if (c.left() != 0)
+        throw std::runtime_error(std::to_string(c.left()) + " stray bytes after the last tensor of " + path);
     return w;
 }
 

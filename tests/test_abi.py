@@ -62,7 +62,7 @@ def test_weights_rejected_before_cuda(tmp_path, capfd):
     bad = tmp_path / "bad.tcw"
     bad.write_bytes(b"NOPE")
     assert not lib.tc_create(str(bad).encode(), 4)
-    assert "tc_create: bad weights file" in capfd.readouterr().err
+    assert "is not a .tcw weight file" in capfd.readouterr().err
     assert not lib.tc_create(str(tmp_path / "missing.tcw").encode(), 4)
     assert "cannot open" in capfd.readouterr().err
     # a well-formed file with a wrong shape names the tensor
@@ -77,7 +77,11 @@ def test_weights_rejected_before_cuda(tmp_path, capfd):
     synth.write_tcw(good, synth.random_weights(0))
     (tmp_path / "trunc.tcw").write_bytes(good.read_bytes()[:1000])
     assert not lib.tc_create(str(tmp_path / "trunc.tcw").encode(), 4)
-    assert "truncated" in capfd.readouterr().err
+    assert "weight file ends at byte 1000" in capfd.readouterr().err
+    # bytes after the last tensor
+    (tmp_path / "tail.tcw").write_bytes(good.read_bytes() + b"xx")
+    assert not lib.tc_create(str(tmp_path / "tail.tcw").encode(), 4)
+    assert "2 stray bytes after the last tensor" in capfd.readouterr().err
     w = synth.random_weights(0)
     del w["dim_reducer.4.bias"]
     synth.write_tcw(tmp_path / "miss.tcw", w)
@@ -154,7 +158,7 @@ def test_tile_driver_cli_without_gpu(tmp_path):
     bad.write_bytes(b"NOPE")
     r = subprocess.run([str(DRIVER), str(tmp_path / "tile"), str(tmp_path / "out"), str(bad)], capture_output=True,
                        text=True)
-    assert r.returncode == 1 and "tc_create: bad weights file" in r.stderr
+    assert r.returncode == 1 and "tc_create:" in r.stderr and "is not a .tcw weight file" in r.stderr
 
 
 def test_host_alloc_rejects_nonpositive():
