@@ -14,7 +14,8 @@ int8 quantisation, for every pixel.
 * N > 1 (under torchrun, one process per GPU): config 2, the same tile split by
   pixel rows (FLOP-balanced) across the ranks; no inter-GPU traffic on the data
   path (a barrier and a max-reduce of the timings only). Total work is fixed,
-  so scaling is "strong".
+  so scaling is "strong". With --config 4, each rank encodes its own whole
+  tile instead (config 4's batch of tiles, one per GPU; scaling "weak").
 * `value` is the whole-job throughput with the tile already resident in HBM;
   `e2e` is the same through tc_encode_tile_rows with pinned host buffers
   (host->device copy of the rank's rows and device->host copy of codes and
@@ -360,10 +361,13 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
                                 device_id=torch.device("cuda", local))
 
-    tile = synth.make_config_tile(args.config)
+    # config 4 is a batch of tiles, one whole tile per GPU (seed 4 + rank): the
+    # work per GPU is fixed as N grows; the other configs split one tile by rows
+    replicas = args.config == 4 and world > 1
+    tile = synth.make_config_tile(args.config, seed=4 + rank) if replicas else synth.make_config_tile(args.config)
     T2, H, W = tile["masks"].shape
     Ta, Td = tile["asc"].shape[0], tile["desc"].shape[0]
-    r0, r1 = rank_rows(tile, rank, world)
+    r0, r1 = (0, H) if replicas else rank_rows(tile, rank, world)
     band = band_arrays(tile, r0, r1)
     R = r1 - r0
     npx_band = R * W
@@ -457,7 +461,8 @@ def main():
     else:
         per_rank = [mine]
 
-    total_px = H * W
+    tile_px = H * W
+    total_px = tile_px * (world if replicas else 1)  # pixels the whole job processes per step
     value = total_px * args.steps / (dev_ms_max / 1000.0)
     e2e_value = total_px * args.steps / (e2e_ms_max / 1000.0) if e2e_ms_max else None
     h2d = tile_bytes(band)
@@ -484,15 +489,17 @@ def main():
     out = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": dev_ms_max / args.steps, "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "scaling": "weak" if replicas else "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": WORKLOAD if args.config == 1 else f"config {args.config}",
                    "chunk_tokens": int(os.environ.get("TC_CHUNK_TOKENS", "524288")),
-                   "pixels": total_px, "split": f"rows FLOP-balanced over {world} GPU(s)",
+                   "pixels": total_px,
+                   "split": (f"one whole tile per GPU (seeds 4..{3 + world})" if replicas
+                             else f"rows FLOP-balanced over {world} GPU(s)"),
                    "weights": "Large, Xavier-uniform seed 0, zero biases",
                    "l2": "inputs (2.2 GB tile) larger than L2; no flush"},
-        "tiles_per_hour": 3600.0 * value / total_px,
+        "tiles_per_hour": 3600.0 * value / tile_px,
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world,
-                "tiles_per_hour": 3600.0 * e2e_value / total_px if e2e_value else None},
+                "tiles_per_hour": 3600.0 * e2e_value / tile_px if e2e_value else None},
         "gpu_launches": int(launches),
         "roofline": {"bound": "tensor", "kernel": "k_gemm_bf16 (tcgen05)",
                      "achieved": gemm_tflops, "peak": peak, "unit": "TFLOP/s",
