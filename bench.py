@@ -496,7 +496,7 @@ def main():
                    "split": (f"one whole tile per GPU (seeds 4..{3 + world})" if replicas
                              else f"rows FLOP-balanced over {world} GPU(s)"),
                    "weights": "Large, Xavier-uniform seed 0, zero biases",
-                   "l2": "inputs (2.2 GB tile) larger than L2; no flush"},
+                   "l2": f"inputs ({tile_bytes(band) / 1e9:.1f} GB per GPU) larger than L2; no flush"},
         "tiles_per_hour": 3600.0 * value / tile_px,
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world,
                 "tiles_per_hour": 3600.0 * e2e_value / tile_px if e2e_value else None},
