@@ -23,6 +23,9 @@
 // Nothing in the product links, loads or runs this file: only tests/,
 // __graft_entry__.smoke() and bench.py's CPU-baseline leg use it, as the checker.
 //
+// TC_ORACLE_FP8 switches on the FP8 accuracy study (see e4m3_round below);
+// unset, the arithmetic is the reference's.
+//
 // TC_ORACLE_DUMP=DIR makes tc_encode write each call's inputs and outputs to
 // DIR/batch_NNNNN.bin (int64 G, T2, T1; f32 s2, s1, out), which is how the
 // reference driver's own batching, padding and standardisation are captured
@@ -92,24 +95,62 @@ std::map<std::string, Tensor> load_weights(const char *path) {  // .tcw, tessera
     return w;
 }
 
+// FP8 ACCURACY STUDY (TC_ORACLE_FP8 = "all" | "ffn"; unset = the reference's
+// bf16 arithmetic). It answers whether an FP8 (e4m3) GEMM variant could keep
+// the parity contract: the chosen Linears take e4m3 operands, weights scaled
+// per output channel and activations per row by max|v| / 448, as an FP8
+// tensor-core GEMM with those scales would. "ffn" applies it to FFN1 / FFN2
+// only, "all" to every Linear of the backbones and the head.
+int g_fp8_mode = 0;  // 0 off, 1 ffn, 2 all
+
+// Round to the nearest e4m3 value (1 sign, 4 exponent bits with bias 7, 3
+// mantissa bits; largest 448, smallest normal 2^-6, subnormal step 2^-9; no
+// infinities), ties to even, saturating at 448 as an FP8 conversion with
+// saturation does.
+float e4m3_round(float x) {
+    if (x == 0.f || !std::isfinite(x)) return x;
+    const float a = std::fabs(x);
+    int e = 0;
+    std::frexp(a, &e);                     // a = m 2^e, m in [0.5, 1)
+    const int ex = std::max(e - 1, -6);    // a in [2^ex, 2^(ex+1)) for normals
+    const float step = std::ldexp(1.f, ex - 3);
+    float q = std::nearbyint(a / step) * step;  // the default rounding mode is to nearest even
+    q = std::min(q, 448.f);
+    return std::copysign(q, x);
+}
+
+// A row (or column) quantised as the FP8 GEMM would see it, back in f32.
+void fp8_quantise(float *v, int64_t n, int64_t stride) {
+    float am = 0.f;
+    for (int64_t i = 0; i < n; ++i) am = std::max(am, std::fabs(v[i * stride]));
+    if (am == 0.f) return;
+    const float s = am / 448.f;
+    for (int64_t i = 0; i < n; ++i) v[i * stride] = e4m3_round(v[i * stride] / s) * s;
+}
+
 // Linear weights packed for the CPU kernel: f32 (exact bf16 values) in
 // column panels of 16: wp[(n/16)][k][16].
 struct Lin {
     int64_t N = 0, K = 0;
     std::vector<float> wp;
     std::vector<float> bias;
+    bool fp8 = false;  // accuracy study only
 };
 
-Lin take_linear(std::map<std::string, Tensor> &W, const std::string &wn, const std::string &bn) {
+Lin take_linear(std::map<std::string, Tensor> &W, const std::string &wn, const std::string &bn, bool fp8 = false) {
     const Tensor &t = W.at(wn);
     Lin l;
     l.N = t.shape[0];
     l.K = t.shape[1];
+    l.fp8 = fp8;
     if (l.N % 16) throw std::runtime_error("linear width not a multiple of 16: " + wn);
     l.wp.resize(l.N * l.K);
-    for (int64_t n = 0; n < l.N; ++n)
-        for (int64_t k = 0; k < l.K; ++k)
-            l.wp[((n / 16) * l.K + k) * 16 + (n % 16)] = bf2f(f2bf(t.data[n * l.K + k]));
+    std::vector<float> row(l.K);
+    for (int64_t n = 0; n < l.N; ++n) {
+        for (int64_t k = 0; k < l.K; ++k) row[k] = bf2f(f2bf(t.data[n * l.K + k]));
+        if (fp8) fp8_quantise(row.data(), l.K, 1);
+        for (int64_t k = 0; k < l.K; ++k) l.wp[((n / 16) * l.K + k) * 16 + (n % 16)] = row[k];
+    }
     l.bias = W.at(bn).data;
     return l;
 }
@@ -124,8 +165,10 @@ __attribute__((target_clones("arch=x86-64-v4", "default"))) void linear(const Li
     std::vector<float> af(4 * K);
     for (int64_t m0 = 0; m0 < M; m0 += 4) {
         const int64_t mr = std::min<int64_t>(4, M - m0);
-        for (int64_t r = 0; r < 4; ++r)
+        for (int64_t r = 0; r < 4; ++r) {
             for (int64_t k = 0; k < K; ++k) af[r * K + k] = r < mr ? bf2f(A[(m0 + r) * K + k]) : 0.f;
+            if (L.fp8) fp8_quantise(af.data() + r * K, K, 1);
+        }
         for (int64_t nb = 0; nb < N; nb += 32) {
             const bool two = nb + 16 < N;
             const float *p0 = L.wp.data() + (nb / 16) * K * 16;
@@ -250,13 +293,14 @@ void init_backbone(std::map<std::string, Tensor> &W, Backbone &bb, const std::st
     bb.w1.resize(w1.data.size());
     for (size_t i = 0; i < w1.data.size(); ++i) bb.w1[i] = rbf(w1.data[i]);
     bb.b1 = W.at(p + ".embedding.0.bias").data;
-    bb.emb2 = take_linear(W, p + ".embedding.2.weight", p + ".embedding.2.bias");
+    const bool all8 = g_fp8_mode == 2, ffn8 = g_fp8_mode >= 1;
+    bb.emb2 = take_linear(W, p + ".embedding.2.weight", p + ".embedding.2.bias", all8);
     for (int l = 0; l < NL; ++l) {
         const std::string L = p + ".transformer_encoder.layers." + std::to_string(l);
-        bb.qkv[l] = take_linear(W, L + ".self_attn.in_proj_weight", L + ".self_attn.in_proj_bias");
-        bb.out[l] = take_linear(W, L + ".self_attn.out_proj.weight", L + ".self_attn.out_proj.bias");
-        bb.ffn1[l] = take_linear(W, L + ".linear1.weight", L + ".linear1.bias");
-        bb.ffn2[l] = take_linear(W, L + ".linear2.weight", L + ".linear2.bias");
+        bb.qkv[l] = take_linear(W, L + ".self_attn.in_proj_weight", L + ".self_attn.in_proj_bias", all8);
+        bb.out[l] = take_linear(W, L + ".self_attn.out_proj.weight", L + ".self_attn.out_proj.bias", all8);
+        bb.ffn1[l] = take_linear(W, L + ".linear1.weight", L + ".linear1.bias", ffn8);
+        bb.ffn2[l] = take_linear(W, L + ".linear2.weight", L + ".linear2.bias", ffn8);
         bb.n1s[l] = W.at(L + ".norm1.weight").data;
         bb.n1b[l] = W.at(L + ".norm1.bias").data;
         bb.n2s[l] = W.at(L + ".norm2.weight").data;
@@ -351,6 +395,8 @@ extern "C" {
 
 void *tc_create(const char *weights_path, int block_pixels) {
     try {
+        if (const char *m = std::getenv("TC_ORACLE_FP8"))
+            g_fp8_mode = std::strcmp(m, "all") == 0 ? 2 : std::strcmp(m, "ffn") == 0 ? 1 : 0;
         auto W = load_weights(weights_path);
         auto c = std::make_unique<Ctx>();
         // the reference's block sizes (tessera_cpu.cpp:486-489): TC_BLOCK pixels
@@ -363,8 +409,8 @@ void *tc_create(const char *weights_path, int block_pixels) {
         if (c->P % P1) throw std::runtime_error("TC_BLOCK_S2 must be a multiple of TC_BLOCK");
         init_backbone(W, c->bb[0], "s2_backbone", 10);
         init_backbone(W, c->bb[1], "s1_backbone", 2);
-        c->red1 = take_linear(W, "dim_reducer.0.weight", "dim_reducer.0.bias");
-        c->red2 = take_linear(W, "dim_reducer.4.weight", "dim_reducer.4.bias");
+        c->red1 = take_linear(W, "dim_reducer.0.weight", "dim_reducer.0.bias", g_fp8_mode == 2);
+        c->red2 = take_linear(W, "dim_reducer.4.weight", "dim_reducer.4.bias", g_fp8_mode == 2);
         c->rln_s = W.at("dim_reducer.1.weight").data;
         c->rln_b = W.at("dim_reducer.1.bias").data;
         c->pe_table.resize(367 * D);
@@ -439,5 +485,8 @@ void tc_profile_dump(void *handle) {
 }
 
 void tc_destroy(void *handle) { delete static_cast<Ctx *>(handle); }
+
+// The e4m3 rounding of the FP8 accuracy study, for its test against torch.
+float tc_oracle_e4m3(float x) { return e4m3_round(x); }
 
 }  // extern "C"

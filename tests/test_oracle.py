@@ -147,3 +147,21 @@ def test_oracle_vs_reference_cuda(case):
     assert m["scale_rel_max"] <= 2.0 ** -6, m
     assert m["cos_min"] >= 0.999, m
     assert m["zero_rows_match"] and m["empty_scale_exact"], m
+
+
+def test_fp8_study_rounding_matches_torch():
+    """The e4m3 rounding of the oracle's FP8 accuracy study (oracle/fp8_study.py)
+    is torch's float8_e4m3fn conversion with saturation at 448."""
+    import ctypes as C
+    torch = pytest.importorskip("torch")
+    from conftest import ORACLE
+    lib = C.CDLL(str(ORACLE / "_build" / "libtessera_oracle.so"))
+    lib.tc_oracle_e4m3.restype = C.c_float
+    lib.tc_oracle_e4m3.argtypes = [C.c_float]
+    rng = np.random.default_rng(3)
+    xs = np.concatenate([rng.standard_normal(4000) * np.exp(rng.uniform(-12, 7, 4000)),
+                         [0.0, 448, 449, 464, 479, 480, 1000, -1000, 2 ** -9, 2 ** -10, 3 * 2 ** -10, 2 ** -6,
+                          1.0625, 1.1875, 232, 248]]).astype(np.float32)
+    ours = np.array([lib.tc_oracle_e4m3(float(x)) for x in xs], np.float32)
+    ref = torch.from_numpy(xs).clamp(-448, 448).to(torch.float8_e4m3fn).to(torch.float32).numpy()
+    np.testing.assert_array_equal(ours, ref)
