@@ -245,8 +245,8 @@ def test_attention_uniform(lib):
     close_bf16(att, attention_ref(qkv, np.arange(P + 1) * T), ulps=3, atol=1e-2)
 
 
-def test_layernorm640(lib):
-    M = 5000
+@pytest.mark.parametrize("M", [1, 15, 17, 5000])
+def test_layernorm640(lib, M):
     g = torch.Generator(device="cuda").manual_seed(13)
     x = (torch.randn(M, 640, device="cuda", generator=g) * 3 + 1).to(torch.bfloat16)
     gam = torch.randn(640, device="cuda", generator=g)
