@@ -501,7 +501,7 @@ def main():
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world,
                 "tiles_per_hour": 3600.0 * e2e_value / tile_px if e2e_value else None},
         "gpu_launches": int(launches),
-        "roofline": {"bound": "tensor", "kernel": "k_gemm_bf16 (tcgen05)",
+        "roofline": {"bound": "tensor", "kernel": "k_gemm_bf16 / k_gemm_bf16_tn (tcgen05)",
                      "achieved": gemm_tflops, "peak": peak, "unit": "TFLOP/s",
                      "frac": gemm_tflops / peak if gemm_tflops else None,
                      "peak_source": f"{peaks['source']} bf16 sustained (kernel timed inside a long step)",

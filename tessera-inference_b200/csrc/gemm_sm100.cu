@@ -386,6 +386,205 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     if (warp == 1) tmem_dealloc(tmem_base, 512);
 }
 
+// ------------------------------------------------------------------ operand-swapped variant
+// out = A W^T computed as its transpose D[feature, token] = W A^T: the weight
+// rows are the UMMA's M side (128 features per tile, so N = 640 is five full
+// tiles) and the activation rows its N side (256 tokens per tile). On a layer
+// with N = 640 the normal tiling needs 256 + 256 + 128 columns, and its
+// 128-wide tile costs as many MMA cycles as a full one once the main loop is
+// long (K = 2560): this variant does no such waste. Same stages, same
+// roles, same bounded waits as k_gemm_bf16; the epilogue transposes through
+// the staging buffer:
+//   lane f of a quadrant holds feature f of 32 tokens (tcgen05.ld 32x32b);
+//   bias is one value per lane; the residual block (32 tokens x 32 features)
+//   is loaded row-wise (8 rows x 64 B per instruction) into the staging
+//   buffer and read back by column; the bf16 results are written by column
+//   and stored by row, so global accesses stay 64-byte row segments.
+// Staging rows are 64 B with 16-byte chunks XOR-swizzled by (row >> 1) & 3,
+// which keeps both the row-wise and the column-wise accesses conflict-free.
+constexpr int TN_BM = 128, TN_BN = 256;  // features x tokens per tile
+using TnCfg = GemmCfg<TN_BN>;            // A stage 128 x 64, B stage 256 x 64: the same bytes
+
+__device__ __forceinline__ int stage_off(int row, int col) {  // byte offset of bf16 (row, col) in a 32 x 32 block
+    return row * 64 + ((((col >> 3) ^ ((row >> 1) & 3))) << 4) + ((col & 7) << 1);
+}
+
+// One epilogue warp of the swapped tile: features f0 .. f0 + 31 (its TMEM lane
+// quadrant, one feature per lane) and token columns [c0, c1) of the tile
+// whose first token is tok0.
+__device__ __forceinline__ bool epilogue_tile_tn(const GemmArgs &p, uint32_t tbase, int f0, int tok0, int c0, int c1,
+                                                 uint8_t *stage, int lane, uint64_t *tfull_bar, uint32_t parity,
+                                                 volatile int *abort_flag) {
+    const int f = f0 + lane;  // this lane's output column
+    const float bias = p.bias ? __ldg(p.bias + f) : 0.f;
+    if (!mbar_wait(tfull_bar, parity, abort_flag, p.status, ERR_WAIT_TMEM_FULL)) return false;
+    tc_fence_after();
+#pragma unroll 1
+    for (int c = c0; c < c1; c += 32) {
+        const int t0 = tok0 + c;  // first token of the group
+        // residual rows t0 .. t0 + 31, features f0 .. f0 + 31, row-wise into the staging buffer
+        if (p.res) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int rr = i * 8 + (lane >> 2), k = lane & 3;
+                uint4 v = make_uint4(0, 0, 0, 0);
+                if (t0 + rr < p.M) v = *reinterpret_cast<const uint4 *>(p.res + (size_t)(t0 + rr) * p.ldr + f0 + k * 8);
+                *reinterpret_cast<uint4 *>(stage + rr * 64 + ((k ^ ((rr >> 1) & 3)) << 4)) = v;
+            }
+            __syncwarp();
+        }
+        uint32_t r[32];
+        tmem_ld16(tbase + (uint32_t)c, *reinterpret_cast<uint32_t(*)[16]>(r));
+        tmem_ld16(tbase + (uint32_t)(c + 16), *reinterpret_cast<uint32_t(*)[16]>(r + 16));
+        tmem_ld_wait();
+        uint16_t o[32];
+#pragma unroll
+        for (int t = 0; t < 32; ++t) {
+            float v = __uint_as_float(r[t]) + bias;
+            if (p.relu) v = fmaxf(v, 0.f);
+            if (p.res) v += __bfloat162float(*reinterpret_cast<const bf16 *>(stage + stage_off(t, lane)));
+            const bf16 h = __float2bfloat16_rn(v);
+            o[t] = *reinterpret_cast<const uint16_t *>(&h);
+        }
+        __syncwarp();  // every lane has read its residual column before the buffer is overwritten
+#pragma unroll
+        for (int t = 0; t < 32; ++t) *reinterpret_cast<uint16_t *>(stage + stage_off(t, lane)) = o[t];
+        __syncwarp();
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int rr = i * 8 + (lane >> 2), k = lane & 3;
+            const uint4 v = *reinterpret_cast<const uint4 *>(stage + rr * 64 + ((k ^ ((rr >> 1) & 3)) << 4));
+            if (t0 + rr < p.M) *reinterpret_cast<uint4 *>(p.out + (size_t)(t0 + rr) * p.ldo + f0 + k * 8) = v;
+        }
+        __syncwarp();
+    }
+    return true;
+}
+
+// tmA: the weights W [N, K] (box 128 rows); tmB: the activations [M, K] (box
+// 256 rows); tmR: the residual [M, N] for the L2 prefetch (box 128 x 128).
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
+    k_gemm_bf16_tn(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmR, GemmArgs p) {
+    constexpr int S = TnCfg::STAGES;
+    constexpr int A_BYTES = TN_BM * BK * 2, B_BYTES = TN_BN * BK * 2;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *sA = smem;
+    uint8_t *sB = smem + S * A_BYTES;
+    uint8_t *staging = smem + S * (A_BYTES + B_BYTES);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(staging + STAGING_BYTES);
+    uint64_t *full = bars, *empty = bars + S, *tfull = bars + 2 * S, *tempty = bars + 2 * S + 2;
+    uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 2 * S + 4);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int num_f = p.N / TN_BM;                      // feature tiles
+    const int num_t = (p.M + TN_BN - 1) / TN_BN;        // token tiles
+    const int ntiles = num_f * num_t;                   // tile t: tokens (t / num_f), features (t % num_f)
+    const int nk = p.K / BK;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < S; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 1); }
+        for (int i = 0; i < 2; ++i) { mbar_init(&tfull[i], 1); mbar_init(&tempty[i], EPI_WARPS); }
+        *abort_flag = 0;
+        fence_mbar_init();
+        prefetch_tensormap(&tmA);
+        prefetch_tensormap(&tmB);
+        if (p.res) prefetch_tensormap(&tmR);
+    }
+    if (warp == 1) { tmem_alloc(tmem_holder, 512); tmem_relinquish(); }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_holder;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int s = 0;
+            uint32_t ph = 0;
+            for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
+                const int f0 = (t % num_f) * TN_BM, tok0 = (t / num_f) * TN_BN;
+                if (p.res) {
+                    tma_prefetch_l2_2d(&tmR, f0, tok0);
+                    tma_prefetch_l2_2d(&tmR, f0, tok0 + 128);
+                }
+                bool ok = true;
+                for (int kb = 0; kb < nk; ++kb) {
+                    if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, p.status, ERR_WAIT_SMEM_EMPTY)) { ok = false; break; }
+                    mbar_arrive_expect_tx(&full[s], (uint32_t)(A_BYTES + B_BYTES));
+                    tma_load_2d(sA + s * A_BYTES, &tmA, kb * BK, f0, &full[s]);
+                    tma_load_2d(sB + s * B_BYTES, &tmB, kb * BK, tok0, &full[s]);
+                    if (++s == S) { s = 0; ph ^= 1; }
+                }
+                if (!ok) break;
+            }
+            for (int i = 0; i < S; ++i) {  // every stage released before exit
+                if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, p.status, ERR_WAIT_SMEM_EMPTY)) break;
+                if (++s == S) { s = 0; ph ^= 1; }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = umma_idesc_bf16(TN_BM, TN_BN);
+            int s = 0;
+            uint32_t ph = 0;
+            int tl = 0;
+            for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++tl) {
+                const int buf = tl & 1;
+                const uint32_t use = (uint32_t)(tl >> 1);
+                if (!mbar_wait(&tempty[buf], (use & 1) ^ 1, abort_flag, p.status, ERR_WAIT_TMEM_EMPTY)) break;
+                tc_fence_after();
+                const uint32_t d = tmem_base + (uint32_t)(buf * TN_BN);
+                bool ok = true;
+                for (int kb = 0; kb < nk; ++kb) {
+                    if (!mbar_wait(&full[s], ph, abort_flag, p.status, ERR_WAIT_TMA_FULL)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint64_t adesc = umma_desc_sw128(smem_u32(sA + s * A_BYTES));
+                    const uint64_t bdesc = umma_desc_sw128(smem_u32(sB + s * B_BYTES));
+#pragma unroll
+                    for (int k = 0; k < BK / UMMA_K; ++k)
+                        umma_bf16(d, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), idesc, (kb | k) != 0 ? 1u : 0u);
+                    umma_commit(&empty[s]);
+                    if (++s == S) { s = 0; ph ^= 1; }
+                }
+                if (!ok) break;
+                umma_commit(&tfull[buf]);
+            }
+        }
+    } else {
+        // epilogue warps 2..9: TMEM lane quadrant (32 features) = warp % 4, token half = (warp - 2) / 4
+        const int quad = warp & 3, e = warp - 2, half = e >> 2;
+        uint8_t *stage = staging + e * (32 * 64);
+        int tl = 0;
+        for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++tl) {
+            const int f0 = (t % num_f) * TN_BM, tok0 = (t / num_f) * TN_BN;
+            // token columns of this half that exist (the last token tile may be partial)
+            const int c0 = half * (TN_BN / 2);
+            const int cend = ((p.M - tok0 + 31) / 32) * 32;
+            const int c1 = c0 + TN_BN / 2 < cend ? c0 + TN_BN / 2 : cend;
+            const int buf = tl & 1;
+            const uint32_t use = (uint32_t)(tl >> 1);
+            const uint32_t tbase = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * TN_BN);
+            if (c0 < c1) {
+                if (!epilogue_tile_tn(p, tbase, f0 + quad * 32, tok0, c0, c1, stage, lane, &tfull[buf], use & 1,
+                                      abort_flag))
+                    break;
+            } else if (!mbar_wait(&tfull[buf], use & 1, abort_flag, p.status, ERR_WAIT_TMEM_FULL)) {
+                break;
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[buf]);
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc(tmem_base, 512);
+}
+
 // ------------------------------------------------------------------ CTA-pair variant
 // tcgen05.mma.cta_group::2 with M = 256: a cluster of two CTAs computes a
 // 256 x BN tile. Each CTA loads its own 128 rows of A and half (BN/2 rows) of
@@ -912,6 +1111,28 @@ template <int BN> static void launch_bn(const GemmArgs &p, const bf16 *A, int ld
     k_gemm_bf16<BN><<<grid, GEMM_THREADS, Cfg::SMEM_BYTES, st>>>(ta, tb, tbt, tr, p);
 }
 
+static void launch_tn(const GemmArgs &p, const bf16 *A, int lda, const bf16 *W, cudaStream_t st, int max_ctas) {
+    static bool attr_set[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!attr_set[dev & 63]) {
+        cudaError_t e = cudaFuncSetAttribute(k_gemm_bf16_tn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             TnCfg::SMEM_BYTES);
+        if (e != cudaSuccess) throw std::runtime_error(std::string("gemm_tn smem attribute: ") + cudaGetErrorString(e));
+        attr_set[dev & 63] = true;
+    }
+    CUtensorMap ta, tb, tr;
+    make_tmap(&ta, W, (uint64_t)p.N, (uint64_t)p.K, (uint64_t)p.K, TN_BM);
+    make_tmap(&tb, A, (uint64_t)p.M, (uint64_t)p.K, (uint64_t)lda, TN_BN);
+    if (p.res) make_tmap_box(&tr, p.res, (uint64_t)p.M, (uint64_t)p.N, (uint64_t)p.ldr, 128, 128, CU_TENSOR_MAP_SWIZZLE_NONE);
+    else tr = ta;
+    const int ntiles = (p.N / TN_BM) * ((p.M + TN_BN - 1) / TN_BN);
+    int grid = std::min(ntiles, num_sms());
+    if (max_ctas > 0) grid = std::min(grid, max_ctas);
+    if (grid < 1) grid = 1;
+    k_gemm_bf16_tn<<<grid, GEMM_THREADS, TnCfg::SMEM_BYTES, st>>>(ta, tb, tr, p);
+}
+
 template <int BN> static void launch_pair(const GemmArgs &p, const bf16 *A, int lda, const bf16 *W, cudaStream_t st,
                                           int max_ctas) {
     using Cfg = Gemm2Cfg<BN>;
@@ -959,13 +1180,27 @@ static void launch_ln(const GemmArgs &p, const bf16 *A, int lda, const bf16 *W, 
     k_gemm_ln640<<<LN_CTAS * clusters, GEMM_THREADS, Cfg::SMEM_BYTES, st>>>(ta, tb, p);
 }
 
-// TC_GEMM_VARIANT=1 forces the single-CTA kernel, 2 the CTA-pair kernel.
+// Kernel choice when launch_gemm is asked for variant 0. Unset, TC_GEMM_VARIANT
+// picks per layer (gemm_auto_variant); 1 forces the single-CTA kernel, 2 the
+// CTA-pair kernel, 3 the operand-swapped kernel wherever N is a multiple of 128.
 int gemm_default_variant() {
     static int v = [] {
         const char *e = std::getenv("TC_GEMM_VARIANT");
-        return e && (*e == '1' || *e == '2') ? *e - '0' : 1;
+        return e && (*e == '1' || *e == '2' || *e == '3') ? *e - '0' : 0;
     }();
     return v;
+}
+
+// The per-layer choice, from sustained timings at M = 524,288 (op_bench.py
+// gemm, same call; the two kernels give bit-identical outputs): the swapped
+// kernel is faster without a residual (QKV 1,334 against 1,479 us, FFN1 1,749
+// against 1,869) and with one behind a long main loop (FFN2, K = 2560: 1,695
+// against 1,766), and much slower for a residual behind a short one
+// (out-proj, K = 640: 916 against 636), where its transposing epilogue is the
+// critical path.
+static int gemm_auto_variant(const GemmArgs &p) {
+    const bool swappable = p.N % TN_BM == 0 && !p.pe_doy && !p.ln_g;
+    return swappable && (!p.res || p.K >= 2048) ? 3 : 1;
 }
 
 int gemm_pick_bn(int N) {
@@ -988,6 +1223,15 @@ void launch_gemm(const GemmArgs &p, const bf16 *A, int lda, const bf16 *W, cudaS
     if (p.M <= 0) return;
     if (p.K % BK) throw std::runtime_error("gemm: K must be a multiple of 64");
     if (variant == 0) variant = gemm_default_variant();
+    if (variant == 0) variant = gemm_auto_variant(p);
+    if (variant == 3) {
+        if (p.N % TN_BM || p.pe_doy || p.ln_g || p.ldo % 8 || (p.res && p.ldr % 8))
+            variant = 1;  // shapes the swapped kernel does not take run on the single-CTA one
+        else {
+            launch_tn(p, A, lda, W, st, max_ctas);
+            return;
+        }
+    }
     if (bn == 0) bn = variant == 2 ? gemm_pick_bn_pair(p.N) : gemm_pick_bn(p.N);
     if (bn == 0 || p.N % 16 || (variant == 2 && p.N % bn))
         throw std::runtime_error("gemm: unsupported N " + std::to_string(p.N));

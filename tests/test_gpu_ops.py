@@ -90,10 +90,12 @@ GEMM_SHAPES = [
 ]
 
 
-@pytest.mark.parametrize("variant", [1, 2])
+@pytest.mark.parametrize("variant", [1, 2, 3])
 @pytest.mark.parametrize("M,N,K", GEMM_SHAPES)
 @pytest.mark.parametrize("mode", ["bias", "bias_relu", "bias_res"])
 def test_gemm(lib, M, N, K, mode, variant):
+    """variant 1: single-CTA tiles; 2: CTA pairs; 3: weights on the MMA's M side
+    (operand-swapped, transposing epilogue)."""
     g = torch.Generator(device="cuda").manual_seed(M * 7 + N * 3 + K)
     A = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
     W = (torch.randn(N, K, device="cuda", generator=g) / K ** 0.5).to(torch.bfloat16)
@@ -383,3 +385,28 @@ def test_gemm_layernorm_fused(lib, M, K):
     # rel 2^-6: one bf16 ulp of the larger of the two values when they straddle a power of two
     check_bf16(out, ref, yf.abs() * rstd * gam.abs() + bet.abs(), rel=2.0 ** -6, acc=2.0 ** -7, atol=1e-4,
                exact_frac=0.9)
+
+
+@pytest.mark.parametrize("M,N,K,mode", [(20000, 640, 2560, "res"), (4099, 640, 640, "relu"), (300, 2560, 640, "bias"),
+                                        (1, 128, 2560, "bias")])
+def test_gemm_swapped_agrees_with_single(lib, M, N, K, mode):
+    """The operand-swapped kernel computes every output from the same products
+    in the same k order as the single-CTA kernel: the two agree to within the
+    GEMM tolerance, and almost every element is bit-identical."""
+    g = torch.Generator(device="cuda").manual_seed(M + N + K)
+    A = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
+    W = (torch.randn(N, K, device="cuda", generator=g) / K ** 0.5).to(torch.bfloat16)
+    bias = torch.randn(N, device="cuda", generator=g) * 0.1
+    res = torch.randn(M, N, device="cuda", generator=g).to(torch.bfloat16) if mode == "res" else None
+    outs = []
+    for variant in (1, 3):
+        out = torch.full((M, N), float("nan"), device="cuda", dtype=torch.bfloat16)
+        status = torch.zeros(1, dtype=torch.int32, device="cuda")
+        assert lib.tcb_op_gemm(_p(A), K, _p(W), _p(bias), int(mode == "relu"), _p(res), N, None, 1, None, None, _p(out),
+                               N, M, N, K, 0, variant, _p(status), _stream()) == 0
+        torch.cuda.synchronize()
+        assert status.item() == 0
+        outs.append(out)
+    ref, mag = gemm_ref(A, W, bias, mode == "relu", res)
+    check_bf16(outs[1], outs[0], mag, exact_frac=0.99)
+    print("bit-identical fraction", (outs[0].view(torch.int16) == outs[1].view(torch.int16)).float().mean().item())
