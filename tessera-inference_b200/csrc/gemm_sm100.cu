@@ -42,14 +42,22 @@ constexpr int EPI_WARPS = 8;      // two per TMEM lane quadrant, splitting the t
 constexpr int STAGING_BYTES = EPI_WARPS * 32 * 64;  // per epilogue warp: 32 rows x 32 bf16
 constexpr int SMEM_BUDGET = 225 * 1024;
 constexpr int RES_BOX = 128;      // residual L2-prefetch box: 128 columns x BM rows
+// The bias vector, copied to shared memory once per CTA by the epilogue warps
+// (N <= BIAS_MAX; wider layers read it from global memory). Read per column
+// group from global memory, the bias loads sat on the epilogue's critical
+// path and made it, not the MMA, the limit of the K = 640 layers.
+constexpr int BIAS_MAX = 2560;
+constexpr int BIAS_BYTES = BIAS_MAX * 4;
+constexpr int BARRIER_BYTES = 256;
 
 template <int BN> struct GemmCfg {
     static constexpr int A_BYTES = BM * BK * 2;
     static constexpr int B_BYTES = BN * BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int STAGES_RAW = (SMEM_BUDGET - 2048 - STAGING_BYTES) / STAGE_BYTES;
+    static constexpr int STAGES_RAW = (SMEM_BUDGET - 2048 - STAGING_BYTES - BIAS_BYTES) / STAGE_BYTES;
     static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
-    static constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * STAGE_BYTES + STAGING_BYTES + 256 /*barriers*/;
+    // align slack, stages, staging, barriers, bias
+    static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + STAGING_BYTES + BARRIER_BYTES + BIAS_BYTES;
     static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N for M=128 must be a multiple of 16 in [16,256]");
     static_assert(B_BYTES % 1024 == 0, "B stage must keep 1024-byte alignment for the 128B swizzle");
     static_assert(STAGES >= 2, "need at least two pipeline stages");
@@ -64,13 +72,36 @@ __device__ __forceinline__ float pe_value(float doy, int n, const bf16 *__restri
 
 // bias, [relu], residual or DOY sinusoid and bf16 rounding of 16 accumulator
 // columns of one output row, packed into two 16-byte words.
+__device__ __forceinline__ float4 lds_f4(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
+    return v;
+}
+
+// The epilogue warps' copy of the bias into shared memory (bias_sa: its
+// shared address), then a barrier among those 8 warps only. Returns the
+// address, or 0 when the bias is read from global memory.
+__device__ __forceinline__ uint32_t stage_bias(const GemmArgs &p, uint8_t *bias_smem) {
+    if (!p.bias || p.N > BIAS_MAX) return 0u;
+    float *sb = reinterpret_cast<float *>(bias_smem);
+    for (int i = threadIdx.x - 64; i < p.N; i += EPI_WARPS * 32) sb[i] = __ldg(p.bias + i);
+    asm volatile("bar.sync 1, %0;" ::"n"(EPI_WARPS * 32) : "memory");
+    return smem_u32(sb);
+}
+
 __device__ __forceinline__ void epilogue_cols16(const GemmArgs &p, const uint32_t (&r)[16], const uint4 (&res)[2],
                                                 bool has_res, float pe_doy, bool pe_tab, int pe_di, int n,
-                                                uint4 (&o)[2], bool pe_irregular) {
+                                                uint4 (&o)[2], bool pe_irregular, uint32_t bias_sa) {
     float v[16];
 #pragma unroll
     for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
-    if (p.bias) {
+    if (bias_sa) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float4 b = lds_f4(bias_sa + (uint32_t)(n + 4 * j) * 4u);
+            v[4 * j] += b.x; v[4 * j + 1] += b.y; v[4 * j + 2] += b.z; v[4 * j + 3] += b.w;
+        }
+    } else if (p.bias) {
         const float4 *b4 = reinterpret_cast<const float4 *>(p.bias + n);
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
@@ -161,7 +192,7 @@ __device__ __forceinline__ void res_stage_group(uint8_t *stage, bool two, int la
 // Returns false if the wait for the accumulator gave up.
 __device__ __forceinline__ bool epilogue_tile(const GemmArgs &p, uint32_t tbase, int row_base, int n0, int c0, int c1,
                                               uint8_t *stage, int lane, uint64_t *tfull_bar, uint32_t parity,
-                                              volatile int *abort_flag) {
+                                              volatile int *abort_flag, uint32_t bias_sa) {
     const int row = row_base + lane;
     const bool live = row < p.M;
     const bf16 *res_row = nullptr;
@@ -215,11 +246,11 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs &p, uint32_t tbase,
         if (two) tmem_ld16(tbase + (uint32_t)(c + 16), r1);
         tmem_ld_wait();
         uint4 o[2];
-        epilogue_cols16(p, r0, q0, res_row != nullptr, pe_doy, false, 0, n0 + c, o, pe_irregular);
+        epilogue_cols16(p, r0, q0, res_row != nullptr, pe_doy, false, 0, n0 + c, o, pe_irregular, bias_sa);
         my_row[0 ^ sw] = o[0];
         my_row[1 ^ sw] = o[1];
         if (two) {
-            epilogue_cols16(p, r1, q1, res_row != nullptr, pe_doy, false, 0, n0 + c + 16, o, pe_irregular);
+            epilogue_cols16(p, r1, q1, res_row != nullptr, pe_doy, false, 0, n0 + c + 16, o, pe_irregular, bias_sa);
             my_row[2 ^ sw] = o[0];
             my_row[3 ^ sw] = o[1];
         }
@@ -364,6 +395,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         // epilogue warps 2..9: TMEM lane quadrant = warp % 4, column half = (warp - 2) / 4
         const int quad = warp & 3, e = warp - 2, half = e >> 2;
         uint8_t *stage = staging + e * (32 * 64);
+        const uint32_t bias_sa = stage_bias(p, staging + STAGING_BYTES + BARRIER_BYTES);
         int tl = 0;
         for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++tl) {
             const int nt = t % num_n, m0 = (t / num_n) * BM, n0 = nt * BN;
@@ -372,7 +404,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             const int buf = tl & 1;
             const uint32_t use = (uint32_t)(tl >> 1);
             const uint32_t tbase = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * BN);
-            if (!epilogue_tile(p, tbase, m0 + quad * 32, n0, c0, c1, stage, lane, &tfull[buf], use & 1, abort_flag))
+            if (!epilogue_tile(p, tbase, m0 + quad * 32, n0, c0, c1, stage, lane, &tfull[buf], use & 1, abort_flag,
+                               bias_sa))
                 break;
             tc_fence_before();
             __syncwarp();
@@ -409,29 +442,43 @@ __device__ __forceinline__ int stage_off(int row, int col) {  // byte offset of 
     return row * 64 + ((((col >> 3) ^ ((row >> 1) & 3))) << 4) + ((col & 7) << 1);
 }
 
+// The residual block of tokens t0 .. t0 + 31, features f0 .. f0 + 31, in the
+// row-wise pattern: g[i] is token i * 8 + lane / 4, 16 bytes at lane % 4
+// (zeros past the last token).
+__device__ __forceinline__ void res_load_tn(const GemmArgs &p, int t0, int f0, int lane, uint4 (&g)[4]) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int rr = i * 8 + (lane >> 2), k = lane & 3;
+        g[i] = t0 + rr < p.M ? *reinterpret_cast<const uint4 *>(p.res + (size_t)(t0 + rr) * p.ldr + f0 + k * 8)
+                             : make_uint4(0, 0, 0, 0);
+    }
+}
+
 // One epilogue warp of the swapped tile: features f0 .. f0 + 31 (its TMEM lane
 // quadrant, one feature per lane) and token columns [c0, c1) of the tile
-// whose first token is tok0.
+// whose first token is tok0. The residual loads run one 32-token group
+// ahead, the first group's before the wait for the accumulator.
 __device__ __forceinline__ bool epilogue_tile_tn(const GemmArgs &p, uint32_t tbase, int f0, int tok0, int c0, int c1,
                                                  uint8_t *stage, int lane, uint64_t *tfull_bar, uint32_t parity,
                                                  volatile int *abort_flag) {
     const int f = f0 + lane;  // this lane's output column
     const float bias = p.bias ? __ldg(p.bias + f) : 0.f;
+    uint4 g[4];
+    if (p.res) res_load_tn(p, tok0 + c0, f0, lane, g);
     if (!mbar_wait(tfull_bar, parity, abort_flag, p.status, ERR_WAIT_TMEM_FULL)) return false;
     tc_fence_after();
 #pragma unroll 1
     for (int c = c0; c < c1; c += 32) {
         const int t0 = tok0 + c;  // first token of the group
-        // residual rows t0 .. t0 + 31, features f0 .. f0 + 31, row-wise into the staging buffer
+        // the group's residual, row-wise into the staging buffer; then the next group's loads
         if (p.res) {
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
                 const int rr = i * 8 + (lane >> 2), k = lane & 3;
-                uint4 v = make_uint4(0, 0, 0, 0);
-                if (t0 + rr < p.M) v = *reinterpret_cast<const uint4 *>(p.res + (size_t)(t0 + rr) * p.ldr + f0 + k * 8);
-                *reinterpret_cast<uint4 *>(stage + rr * 64 + ((k ^ ((rr >> 1) & 3)) << 4)) = v;
+                *reinterpret_cast<uint4 *>(stage + rr * 64 + ((k ^ ((rr >> 1) & 3)) << 4)) = g[i];
             }
             __syncwarp();
+            if (c + 32 < c1) res_load_tn(p, t0 + 32, f0, lane, g);
         }
         uint32_t r[32];
         tmem_ld16(tbase + (uint32_t)c, *reinterpret_cast<uint32_t(*)[16]>(r));
@@ -599,9 +646,9 @@ template <int BN> struct Gemm2Cfg {
     static constexpr int A_BYTES = BM * BK * 2;
     static constexpr int B_BYTES = BNH * BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int STAGES_RAW = (SMEM_BUDGET - 2048 - STAGING_BYTES) / STAGE_BYTES;
+    static constexpr int STAGES_RAW = (SMEM_BUDGET - 2048 - STAGING_BYTES - BIAS_BYTES) / STAGE_BYTES;
     static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
-    static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + STAGING_BYTES + 256;
+    static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + STAGING_BYTES + BARRIER_BYTES + BIAS_BYTES;
     static_assert(BN % 16 == 0 && BN >= 32 && BN <= 256, "pair UMMA N must be a multiple of 16 in [32, 256]");
     static_assert(B_BYTES % 1024 == 0, "B stage must keep 1024-byte alignment for the 128B swizzle");
 };
@@ -701,6 +748,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
         const int quad = warp & 3, e = warp - 2, half = e >> 2;
         const int c0 = half ? epi_split<BN>() : 0, c1 = half ? BN : epi_split<BN>();
         uint8_t *stage = staging + e * (32 * 64);
+        const uint32_t bias_sa = stage_bias(p, staging + STAGING_BYTES + BARRIER_BYTES);
         int tl = 0;
         for (int t = pair; t < ntiles; t += npairs, ++tl) {
             const int buf = tl & 1;
@@ -708,7 +756,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
             const int row_base = (t / num_n) * (2 * BM) + (int)rank * BM + quad * 32;
             const uint32_t tbase = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * BN);
             if (!epilogue_tile(p, tbase, row_base, (t % num_n) * BN, c0, c1, stage, lane, &tfull[buf], use & 1,
-                               abort_flag))
+                               abort_flag, bias_sa))
                 break;
             tc_fence_before();
             __syncwarp();

@@ -115,7 +115,7 @@ def main(argv=None) -> int:
     ap.add_argument("--N", type=int, default=2560)
     ap.add_argument("--K", type=int, default=640)
     ap.add_argument("--mode", choices=["bias", "relu", "res"], default="relu")
-    ap.add_argument("--variant", type=int, default=0, help="0 default, 1 single CTA, 2 CTA pair")
+    ap.add_argument("--variant", type=int, default=0, help="0 per-layer choice, 1 single CTA, 2 CTA pair, 3 operand-swapped")
     ap.add_argument("--seconds", type=float, default=3.0)
     ap.add_argument("--torch", action="store_true", help="also time torch.matmul (cuBLAS) on the same shape")
     ap.add_argument("--T", type=int, default=120, help="uniform series length (attention)")
