@@ -102,6 +102,24 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *tm, in
         : "memory");
 }
 
+// Bulk tensor store of one shared-memory box to global memory, in the bulk
+// async-group of the issuing thread (coordinates are never negative; rows past
+// the tensor's extent are not written). The source must not be overwritten
+// before bulk_wait_read0() in the same thread, and generic-proxy writes to it
+// must be made visible first with fence_proxy_async_smem().
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap *tm, const void *src, int c0, int c1) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                     reinterpret_cast<uint64_t>(tm)),
+                 "r"(c0), "r"(c1), "r"(smem_u32(src))
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// every committed bulk store of this thread has read its shared-memory source
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// every committed bulk store of this thread is complete
+__device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
 // Prefetch one box of a tensor map into L2 (no shared memory, nothing to wait for).
 __device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap *tm, int c0, int c1) {
     asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(reinterpret_cast<uint64_t>(tm)),

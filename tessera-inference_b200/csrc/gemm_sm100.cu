@@ -181,8 +181,12 @@ __device__ __forceinline__ void res_stage_group(uint8_t *stage, bool two, int la
 // quadrant, one row per lane) and accumulator columns [c0, c1) of a tile whose
 // first output column is n0. Per group of 32 columns: TMEM -> registers ->
 // epilogue math -> a 2 KB staging buffer (32 rows x 64 B, 16-byte chunks XOR-
-// swizzled so both the row-wise writes and the read-back are conflict-free) ->
-// row-contiguous 64-byte global stores, 8 rows per instruction.
+// swizzled by (row >> 1) & 3, which is the TMA 64-byte swizzle) -> one bulk
+// tensor store of the 32 x 32 block (tmO), issued by lane 0. Issued by the
+// warp as 8-row x 64-byte global stores instead, the output cost about a
+// fifth of the FFN1 launch's time; the bulk store takes it off the warps.
+// A 16-column group (a tile width that is not a multiple of 32) is stored by
+// the warp, 16 rows x 32 bytes per instruction.
 // The residual (or, for an integer day of year, the DOY-table row, which is
 // an ordinary residual row) takes the same way in reverse: loaded 8 rows x 64
 // contiguous bytes per instruction (the row pointers passed between lanes by
@@ -192,7 +196,7 @@ __device__ __forceinline__ void res_stage_group(uint8_t *stage, bool two, int la
 // Returns false if the wait for the accumulator gave up.
 __device__ __forceinline__ bool epilogue_tile(const GemmArgs &p, uint32_t tbase, int row_base, int n0, int c0, int c1,
                                               uint8_t *stage, int lane, uint64_t *tfull_bar, uint32_t parity,
-                                              volatile int *abort_flag, uint32_t bias_sa) {
+                                              volatile int *abort_flag, uint32_t bias_sa, const CUtensorMap *tmO) {
     const int row = row_base + lane;
     const bool live = row < p.M;
     const bf16 *res_row = nullptr;
@@ -227,6 +231,9 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs &p, uint32_t tbase,
         const bool two = c + 32 <= c1;
         uint4 q[4] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
         if (any_res) {
+            // the staging buffer is free once the previous group's bulk store has read it
+            if (lane == 0) bulk_wait_read0();
+            __syncwarp();
             // the group's residual, from the coalesced layout to one row per lane
             res_stage_group(stage, two, lane, g0, g1, g2, g3);
             __syncwarp();
@@ -245,25 +252,27 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs &p, uint32_t tbase,
         tmem_ld16(tbase + (uint32_t)c, r0);
         if (two) tmem_ld16(tbase + (uint32_t)(c + 16), r1);
         tmem_ld_wait();
-        uint4 o[2];
+        uint4 o[2], o1[2];
         epilogue_cols16(p, r0, q0, res_row != nullptr, pe_doy, false, 0, n0 + c, o, pe_irregular, bias_sa);
+        if (two)
+            epilogue_cols16(p, r1, q1, res_row != nullptr, pe_doy, false, 0, n0 + c + 16, o1, pe_irregular, bias_sa);
+        if (!any_res) {  // the staging buffer is free once the previous group's bulk store has read it
+            if (lane == 0) bulk_wait_read0();
+            __syncwarp();
+        }
         my_row[0 ^ sw] = o[0];
         my_row[1 ^ sw] = o[1];
         if (two) {
-            epilogue_cols16(p, r1, q1, res_row != nullptr, pe_doy, false, 0, n0 + c + 16, o, pe_irregular, bias_sa);
-            my_row[2 ^ sw] = o[0];
-            my_row[3 ^ sw] = o[1];
-        }
-        __syncwarp();
-        if (two) {
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const int rr = i * 8 + (lane >> 2), k = lane & 3;
-                const uint4 v = reinterpret_cast<const uint4 *>(stage + rr * 64)[k ^ ((rr >> 1) & 3)];
-                if (row_base + rr < p.M)
-                    *reinterpret_cast<uint4 *>(p.out + (size_t)(row_base + rr) * p.ldo + n0 + c + k * 8) = v;
+            my_row[2 ^ sw] = o1[0];
+            my_row[3 ^ sw] = o1[1];
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0 && row_base < p.M) {  // rows past M are clipped; a block wholly past M is skipped
+                tma_store_2d(tmO, stage, n0 + c, row_base);
+                bulk_commit();
             }
         } else {
+            __syncwarp();
 #pragma unroll
             for (int i = 0; i < 2; ++i) {
                 const int rr = i * 16 + (lane >> 1), k = lane & 1;
@@ -271,8 +280,8 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs &p, uint32_t tbase,
                 if (row_base + rr < p.M)
                     *reinterpret_cast<uint4 *>(p.out + (size_t)(row_base + rr) * p.ldo + n0 + c + k * 8) = v;
             }
+            __syncwarp();
         }
-        __syncwarp();
     }
     return true;
 }
@@ -294,7 +303,8 @@ template <int BN> __host__ __device__ constexpr int epi_split() { return epi_spl
 template <int BN>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     k_gemm_bf16(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                const __grid_constant__ CUtensorMap tmBt, const __grid_constant__ CUtensorMap tmR, GemmArgs p) {
+                const __grid_constant__ CUtensorMap tmBt, const __grid_constant__ CUtensorMap tmR,
+                const __grid_constant__ CUtensorMap tmO, GemmArgs p) {
     using Cfg = GemmCfg<BN>;
     constexpr int S = Cfg::STAGES;
     extern __shared__ uint8_t smem_raw[];
@@ -405,12 +415,13 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             const uint32_t use = (uint32_t)(tl >> 1);
             const uint32_t tbase = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * BN);
             if (!epilogue_tile(p, tbase, m0 + quad * 32, n0, c0, c1, stage, lane, &tfull[buf], use & 1, abort_flag,
-                               bias_sa))
+                               bias_sa, &tmO))
                 break;
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tempty[buf]);
         }
+        if (lane == 0) bulk_wait0();  // this warp's output stores are complete before the CTA exits
     }
 
     tc_fence_before();
@@ -457,10 +468,12 @@ __device__ __forceinline__ void res_load_tn(const GemmArgs &p, int t0, int f0, i
 // One epilogue warp of the swapped tile: features f0 .. f0 + 31 (its TMEM lane
 // quadrant, one feature per lane) and token columns [c0, c1) of the tile
 // whose first token is tok0. The residual loads run one 32-token group
-// ahead, the first group's before the wait for the accumulator.
+// ahead, the first group's before the wait for the accumulator. Each group's
+// 32 tokens x 32 features leave the staging buffer by one bulk tensor store
+// (tmO) issued by lane 0.
 __device__ __forceinline__ bool epilogue_tile_tn(const GemmArgs &p, uint32_t tbase, int f0, int tok0, int c0, int c1,
                                                  uint8_t *stage, int lane, uint64_t *tfull_bar, uint32_t parity,
-                                                 volatile int *abort_flag) {
+                                                 volatile int *abort_flag, const CUtensorMap *tmO) {
     const int f = f0 + lane;  // this lane's output column
     const float bias = p.bias ? __ldg(p.bias + f) : 0.f;
     uint4 g[4];
@@ -472,6 +485,9 @@ __device__ __forceinline__ bool epilogue_tile_tn(const GemmArgs &p, uint32_t tba
         const int t0 = tok0 + c;  // first token of the group
         // the group's residual, row-wise into the staging buffer; then the next group's loads
         if (p.res) {
+            // the staging buffer is free once the previous group's bulk store has read it
+            if (lane == 0) bulk_wait_read0();
+            __syncwarp();
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
                 const int rr = i * 8 + (lane >> 2), k = lane & 3;
@@ -494,16 +510,18 @@ __device__ __forceinline__ bool epilogue_tile_tn(const GemmArgs &p, uint32_t tba
             o[t] = *reinterpret_cast<const uint16_t *>(&h);
         }
         __syncwarp();  // every lane has read its residual column before the buffer is overwritten
+        if (!p.res) {  // the staging buffer is free once the previous group's bulk store has read it
+            if (lane == 0) bulk_wait_read0();
+            __syncwarp();
+        }
 #pragma unroll
         for (int t = 0; t < 32; ++t) *reinterpret_cast<uint16_t *>(stage + stage_off(t, lane)) = o[t];
+        fence_proxy_async_smem();
         __syncwarp();
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const int rr = i * 8 + (lane >> 2), k = lane & 3;
-            const uint4 v = *reinterpret_cast<const uint4 *>(stage + rr * 64 + ((k ^ ((rr >> 1) & 3)) << 4));
-            if (t0 + rr < p.M) *reinterpret_cast<uint4 *>(p.out + (size_t)(t0 + rr) * p.ldo + f0 + k * 8) = v;
+        if (lane == 0) {
+            tma_store_2d(tmO, stage, f0, t0);
+            bulk_commit();
         }
-        __syncwarp();
     }
     return true;
 }
@@ -512,7 +530,7 @@ __device__ __forceinline__ bool epilogue_tile_tn(const GemmArgs &p, uint32_t tba
 // 256 rows); tmR: the residual [M, N] for the L2 prefetch (box 128 x 128).
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     k_gemm_bf16_tn(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const __grid_constant__ CUtensorMap tmR, GemmArgs p) {
+                   const __grid_constant__ CUtensorMap tmR, const __grid_constant__ CUtensorMap tmO, GemmArgs p) {
     constexpr int S = TnCfg::STAGES;
     constexpr int A_BYTES = TN_BM * BK * 2, B_BYTES = TN_BN * BK * 2;
     extern __shared__ uint8_t smem_raw[];
@@ -615,7 +633,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             const uint32_t tbase = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * TN_BN);
             if (c0 < c1) {
                 if (!epilogue_tile_tn(p, tbase, f0 + quad * 32, tok0, c0, c1, stage, lane, &tfull[buf], use & 1,
-                                      abort_flag))
+                                      abort_flag, &tmO))
                     break;
             } else if (!mbar_wait(&tfull[buf], use & 1, abort_flag, p.status, ERR_WAIT_TMEM_FULL)) {
                 break;
@@ -624,6 +642,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(&tempty[buf]);
         }
+        if (lane == 0) bulk_wait0();
     }
 
     tc_fence_before();
@@ -655,7 +674,8 @@ template <int BN> struct Gemm2Cfg {
 
 template <int BN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
-    k_gemm2_bf16(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs p) {
+    k_gemm2_bf16(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                 const __grid_constant__ CUtensorMap tmO, GemmArgs p) {
     using Cfg = Gemm2Cfg<BN>;
     constexpr int S = Cfg::STAGES;
     extern __shared__ uint8_t smem_raw[];
@@ -756,12 +776,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
             const int row_base = (t / num_n) * (2 * BM) + (int)rank * BM + quad * 32;
             const uint32_t tbase = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * BN);
             if (!epilogue_tile(p, tbase, row_base, (t % num_n) * BN, c0, c1, stage, lane, &tfull[buf], use & 1,
-                               abort_flag, bias_sa))
+                               abort_flag, bias_sa, &tmO))
                 break;
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[buf]), 0));
         }
+        if (lane == 0) bulk_wait0();
     }
 
     tc_fence_before();
@@ -1118,6 +1139,12 @@ static void make_tmap(CUtensorMap *tm, const void *ptr, uint64_t rows, uint64_t 
     make_tmap_box(tm, ptr, rows, cols, ld_elems, BK, box_rows, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
+// The output map of the bulk stores: [M, N] with pitch ldo, boxes of 32 rows x
+// 32 columns (64 bytes, the 64-byte swizzle of the staging buffers).
+static void make_tmap_out(CUtensorMap *tm, const GemmArgs &p) {
+    make_tmap_box(tm, p.out, (uint64_t)p.M, (uint64_t)p.N, (uint64_t)p.ldo, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
+}
+
 static int num_sms() {
     static int n = 0;
     if (!n) {
@@ -1156,7 +1183,9 @@ template <int BN> static void launch_bn(const GemmArgs &p, const bf16 *A, int ld
     int grid = std::min(ntiles, num_sms());
     if (max_ctas > 0) grid = std::min(grid, max_ctas);
     if (grid < 1) grid = 1;
-    k_gemm_bf16<BN><<<grid, GEMM_THREADS, Cfg::SMEM_BYTES, st>>>(ta, tb, tbt, tr, p);
+    CUtensorMap to;
+    make_tmap_out(&to, p);
+    k_gemm_bf16<BN><<<grid, GEMM_THREADS, Cfg::SMEM_BYTES, st>>>(ta, tb, tbt, tr, to, p);
 }
 
 static void launch_tn(const GemmArgs &p, const bf16 *A, int lda, const bf16 *W, cudaStream_t st, int max_ctas) {
@@ -1178,7 +1207,9 @@ static void launch_tn(const GemmArgs &p, const bf16 *A, int lda, const bf16 *W, 
     int grid = std::min(ntiles, num_sms());
     if (max_ctas > 0) grid = std::min(grid, max_ctas);
     if (grid < 1) grid = 1;
-    k_gemm_bf16_tn<<<grid, GEMM_THREADS, TnCfg::SMEM_BYTES, st>>>(ta, tb, tr, p);
+    CUtensorMap to;
+    make_tmap_out(&to, p);
+    k_gemm_bf16_tn<<<grid, GEMM_THREADS, TnCfg::SMEM_BYTES, st>>>(ta, tb, tr, to, p);
 }
 
 template <int BN> static void launch_pair(const GemmArgs &p, const bf16 *A, int lda, const bf16 *W, cudaStream_t st,
@@ -1200,7 +1231,9 @@ template <int BN> static void launch_pair(const GemmArgs &p, const bf16 *A, int 
     int pairs = std::min(ntiles, num_sms() / 2);
     if (max_ctas > 0) pairs = std::min(pairs, std::max(1, max_ctas / 2));
     if (pairs < 1) pairs = 1;
-    k_gemm2_bf16<BN><<<2 * pairs, GEMM_THREADS, Cfg::SMEM_BYTES, st>>>(ta, tb, p);
+    CUtensorMap to;
+    make_tmap_out(&to, p);
+    k_gemm2_bf16<BN><<<2 * pairs, GEMM_THREADS, Cfg::SMEM_BYTES, st>>>(ta, tb, to, p);
 }
 
 static void launch_ln(const GemmArgs &p, const bf16 *A, int lda, const bf16 *W, cudaStream_t st) {
