@@ -54,11 +54,11 @@ UNIT = "px/s"
 WORKLOAD = "config 1: synthetic Manchester-sized tile 1113x695 (773,535 px), T2=120 (60% valid), Ta=Td=60"
 # DRAM bytes per GEMM FLOP: dram__bytes_read.sum + dram__bytes_write.sum summed
 # over the 1,587 GEMM launches of one ncu capture of a config-1 band (64 rows of
-# a tile with config 1's series and value distributions; 832.8 GB for 3.751e14
+# a tile with config 1's series and value distributions; 842.0 GB for 3.751e14
 # FLOP; profiles/launch_list_config1_band.md), and the algorithmic bytes per
 # FLOP of the same launches (per token emb2 2,560 B and per layer QKV 5,120 B,
 # out-proj 3,840 B, FFN1 6,400 B, FFN2 7,680 B; 8.851e11 B).
-GEMM_DRAM_BYTES_PER_FLOP = 2.22e-3
+GEMM_DRAM_BYTES_PER_FLOP = 2.245e-3
 GEMM_ALG_BYTES_PER_FLOP = 2.36e-3
 SMI_FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
