@@ -792,6 +792,145 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
     if (warp == 1) tmem_dealloc_pair(tmem_base, 512);
 }
 
+// ------------------------------------------------------------------ operand-swapped CTA pair
+// The swapped tiling on a CTA pair (tcgen05.mma.cta_group::2, M = 256): a
+// cluster of two CTAs computes 256 features x 256 tokens. CTA r loads its own
+// 128 weight rows (features fp * 256 + 128 r) and its half of the tile's
+// tokens (tok0 + 128 r), so a CTA moves 32 KB of operands per 64-deep k-block
+// for the same MMA work as the single-CTA swapped kernel's 48 KB. Barriers
+// and roles are those of k_gemm2_bf16; each CTA's epilogue drains its 128
+// features x 256 tokens with the swapped epilogue. When N is an odd multiple
+// of 128, the last pair's second CTA has no features: its weight loads read
+// the tensor map's zero fill past N, and its epilogue stores nothing.
+// Layers with a residual are not run on this kernel.
+using Tn2Cfg = Gemm2Cfg<256>;  // per CTA and stage: 128 weight rows and 128 tokens, 64 deep
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM_THREADS, 1)
+    k_gemm2_bf16_tn(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    const __grid_constant__ CUtensorMap tmO, GemmArgs p) {
+    using Cfg = Tn2Cfg;
+    constexpr int S = Cfg::STAGES;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *sA = smem;
+    uint8_t *sB = smem + S * Cfg::A_BYTES;
+    uint8_t *staging = smem + S * Cfg::STAGE_BYTES;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(staging + STAGING_BYTES);
+    uint64_t *full = bars, *empty = bars + S, *tfull = bars + 2 * S, *tempty = bars + 2 * S + 2;
+    uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 2 * S + 4);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+    const int num_fp = (p.N + 2 * TN_BM - 1) / (2 * TN_BM);  // feature pairs
+    const int num_t = (p.M + TN_BN - 1) / TN_BN;             // token tiles
+    const int ntiles = num_fp * num_t;                        // tile t: tokens t / num_fp, features t % num_fp
+    const int nk = p.K / BK;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < S; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 1); }
+        for (int i = 0; i < 2; ++i) { mbar_init(&tfull[i], 1); mbar_init(&tempty[i], 2 * EPI_WARPS); }
+        *abort_flag = 0;
+        fence_mbar_init();
+        prefetch_tensormap(&tmA);
+        prefetch_tensormap(&tmB);
+    }
+    if (warp == 1) { tmem_alloc_pair(tmem_holder, 512); tmem_relinquish_pair(); }
+    tc_fence_before();
+    cluster_sync();  // both CTAs' barriers exist before any cross-CTA signal
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_holder;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int s = 0;
+            uint32_t ph = 0;
+            for (int t = pair; t < ntiles; t += npairs) {
+                const int f0 = (t % num_fp) * (2 * TN_BM) + (int)rank * TN_BM;
+                const int tok0 = (t / num_fp) * TN_BN + (int)rank * (TN_BN / 2);
+                bool ok = true;
+                for (int kb = 0; kb < nk; ++kb) {
+                    if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, p.status, ERR_WAIT_SMEM_EMPTY)) { ok = false; break; }
+                    const uint32_t fbar = mapa_shared(smem_u32(&full[s]), 0);
+                    if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * Cfg::STAGE_BYTES);
+                    tma_load_2d_pair(sA + s * Cfg::A_BYTES, &tmA, kb * BK, f0, fbar);
+                    tma_load_2d_pair(sB + s * Cfg::B_BYTES, &tmB, kb * BK, tok0, fbar);
+                    if (++s == S) { s = 0; ph ^= 1; }
+                }
+                if (!ok) break;
+            }
+            for (int i = 0; i < S; ++i) {  // tail: every stage released before exit
+                if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, p.status, ERR_WAIT_SMEM_EMPTY)) break;
+                if (++s == S) { s = 0; ph ^= 1; }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && rank == 0) {
+            constexpr uint32_t idesc = umma_idesc_bf16(2 * TN_BM, TN_BN);
+            int s = 0;
+            uint32_t ph = 0;
+            int tl = 0;
+            for (int t = pair; t < ntiles; t += npairs, ++tl) {
+                const int buf = tl & 1;
+                const uint32_t use = (uint32_t)(tl >> 1);
+                if (!mbar_wait(&tempty[buf], (use & 1) ^ 1, abort_flag, p.status, ERR_WAIT_TMEM_EMPTY)) break;
+                tc_fence_after();
+                const uint32_t d = tmem_base + (uint32_t)(buf * TN_BN);
+                bool ok = true;
+                for (int kb = 0; kb < nk; ++kb) {
+                    if (!mbar_wait(&full[s], ph, abort_flag, p.status, ERR_WAIT_TMA_FULL)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint64_t adesc = umma_desc_sw128(smem_u32(sA + s * Cfg::A_BYTES));
+                    const uint64_t bdesc = umma_desc_sw128(smem_u32(sB + s * Cfg::B_BYTES));
+#pragma unroll
+                    for (int k = 0; k < BK / UMMA_K; ++k)
+                        umma_bf16_pair(d, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), idesc,
+                                       (kb | k) != 0 ? 1u : 0u);
+                    umma_commit_pair(mapa_shared(smem_u32(&empty[s]), 0));
+                    umma_commit_pair(mapa_shared(smem_u32(&empty[s]), 1));
+                    if (++s == S) { s = 0; ph ^= 1; }
+                }
+                if (!ok) break;
+                umma_commit_pair(mapa_shared(smem_u32(&tfull[buf]), 0));
+                umma_commit_pair(mapa_shared(smem_u32(&tfull[buf]), 1));
+            }
+        }
+    } else {
+        // epilogue warps 2..9: TMEM lane quadrant (32 features) = warp % 4, token half = (warp - 2) / 4
+        const int quad = warp & 3, e = warp - 2, half = e >> 2;
+        uint8_t *stage = staging + e * (32 * 64);
+        int tl = 0;
+        for (int t = pair; t < ntiles; t += npairs, ++tl) {
+            const int f0 = (t % num_fp) * (2 * TN_BM) + (int)rank * TN_BM;  // this CTA's first feature
+            const int tok0 = (t / num_fp) * TN_BN;
+            const int c0 = half * (TN_BN / 2);
+            const int cend = ((p.M - tok0 + 31) / 32) * 32;
+            const int c1 = c0 + TN_BN / 2 < cend ? c0 + TN_BN / 2 : cend;
+            const int buf = tl & 1;
+            const uint32_t use = (uint32_t)(tl >> 1);
+            const uint32_t tbase = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * TN_BN);
+            if (f0 < p.N && c0 < c1) {
+                if (!epilogue_tile_tn(p, tbase, f0 + quad * 32, tok0, c0, c1, stage, lane, &tfull[buf], use & 1,
+                                      abort_flag, &tmO))
+                    break;
+            } else if (!mbar_wait(&tfull[buf], use & 1, abort_flag, p.status, ERR_WAIT_TMEM_FULL)) {
+                break;
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[buf]), 0));
+        }
+        if (lane == 0) bulk_wait0();
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();  // no CTA leaves while its peer may still signal its barriers or use its TMEM
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc_pair(tmem_base, 512);
+}
+
 // ------------------------------------------------------------------ LayerNorm-fused variant (N = 640)
 // A cluster of four CTAs owns one 128-row block of the 640-column output;
 // cluster rank r computes columns [160 r, 160 r + 160) with the single-CTA
@@ -1236,6 +1375,29 @@ template <int BN> static void launch_pair(const GemmArgs &p, const bf16 *A, int 
     k_gemm2_bf16<BN><<<2 * pairs, GEMM_THREADS, Cfg::SMEM_BYTES, st>>>(ta, tb, to, p);
 }
 
+static void launch_tn_pair(const GemmArgs &p, const bf16 *A, int lda, const bf16 *W, cudaStream_t st, int max_ctas) {
+    using Cfg = Tn2Cfg;
+    static bool attr_set[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!attr_set[dev & 63]) {
+        cudaError_t e =
+            cudaFuncSetAttribute(k_gemm2_bf16_tn, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
+        if (e != cudaSuccess) throw std::runtime_error(std::string("gemm2_tn smem attribute: ") + cudaGetErrorString(e));
+        attr_set[dev & 63] = true;
+    }
+    CUtensorMap ta, tb;
+    make_tmap(&ta, W, (uint64_t)p.N, (uint64_t)p.K, (uint64_t)p.K, TN_BM);
+    make_tmap(&tb, A, (uint64_t)p.M, (uint64_t)p.K, (uint64_t)lda, TN_BN / 2);
+    const int ntiles = ((p.N + 2 * TN_BM - 1) / (2 * TN_BM)) * ((p.M + TN_BN - 1) / TN_BN);
+    int pairs = std::min(ntiles, num_sms() / 2);
+    if (max_ctas > 0) pairs = std::min(pairs, std::max(1, max_ctas / 2));
+    if (pairs < 1) pairs = 1;
+    CUtensorMap to;
+    make_tmap_out(&to, p);
+    k_gemm2_bf16_tn<<<2 * pairs, GEMM_THREADS, Cfg::SMEM_BYTES, st>>>(ta, tb, to, p);
+}
+
 static void launch_ln(const GemmArgs &p, const bf16 *A, int lda, const bf16 *W, cudaStream_t st) {
     using Cfg = GemmLnCfg;
     static int max_clusters[64] = {};
@@ -1267,7 +1429,7 @@ static void launch_ln(const GemmArgs &p, const bf16 *A, int lda, const bf16 *W, 
 int gemm_default_variant() {
     static int v = [] {
         const char *e = std::getenv("TC_GEMM_VARIANT");
-        return e && (*e == '1' || *e == '2' || *e == '3') ? *e - '0' : 0;
+        return e && *e >= '1' && *e <= '4' ? *e - '0' : 0;
     }();
     return v;
 }
@@ -1279,8 +1441,22 @@ int gemm_default_variant() {
 // against 1,766), and much slower for a residual behind a short one
 // (out-proj, K = 640: 916 against 636), where its transposing epilogue is the
 // critical path.
+// TC_GEMM_TN_PAIR=1 runs the layers without a residual on the CTA-pair form of
+// the swapped kernel (read once). Off by default: on the config-1 step (A/B in
+// one call) FFN1 ran at 1,060 against 1,043 TFLOP/s but QKV, whose 1,920
+// features leave the last pair half empty, at 999 against 1,038, and the step
+// at 106.5-106.9k against 107.0-107.1k px/s.
+static bool tn_pair_enabled() {
+    static const bool on = [] {
+        const char *e = std::getenv("TC_GEMM_TN_PAIR");
+        return e && *e == '1';
+    }();
+    return on;
+}
+
 static int gemm_auto_variant(const GemmArgs &p) {
     const bool swappable = p.N % TN_BM == 0 && !p.pe_doy && !p.ln_g;
+    if (swappable && !p.res && tn_pair_enabled()) return 4;
     return swappable && (!p.res || p.K >= 2048) ? 3 : 1;
 }
 
@@ -1305,11 +1481,13 @@ void launch_gemm(const GemmArgs &p, const bf16 *A, int lda, const bf16 *W, cudaS
     if (p.K % BK) throw std::runtime_error("gemm: K must be a multiple of 64");
     if (variant == 0) variant = gemm_default_variant();
     if (variant == 0) variant = gemm_auto_variant(p);
-    if (variant == 3) {
+    if (variant == 4 && p.res) variant = 3;  // the swapped pair takes no residual
+    if (variant == 3 || variant == 4) {
         if (p.N % TN_BM || p.pe_doy || p.ln_g || p.ldo % 8 || (p.res && p.ldr % 8))
-            variant = 1;  // shapes the swapped kernel does not take run on the single-CTA one
+            variant = 1;  // shapes the swapped kernels do not take run on the single-CTA one
         else {
-            launch_tn(p, A, lda, W, st, max_ctas);
+            if (variant == 4) launch_tn_pair(p, A, lda, W, st, max_ctas);
+            else launch_tn(p, A, lda, W, st, max_ctas);
             return;
         }
     }

@@ -44,14 +44,17 @@ int gemm_pick_bn(int N);
 // Kernel forced by TC_GEMM_VARIANT for launch_gemm's variant 0, or 0 when the
 // choice is per layer: 1 = single CTA (M = 128 token tiles), 2 = CTA pair
 // (cta_group::2, M = 256 tiles), 3 = operand-swapped (the weights on the MMA's
-// M side, 128 features x 256 tokens per tile).
+// M side, 128 features x 256 tokens per tile), 4 = operand-swapped CTA pair
+// (256 features x 256 tokens per pair; layers with a residual run on 3).
 int gemm_default_variant();
 
 // Enqueue one GEMM on `st`. bn = 0 picks the tile width; max_ctas > 0 caps the
-// persistent grid; variant 0 = per layer (the operand-swapped kernel when N is
-// a multiple of 128 and there is no residual or K >= 2048, else the single-CTA
-// one), 1 = single CTA, 2 = CTA pair, 3 = operand-swapped. The operand-swapped
-// kernel gives the single-CTA kernel's bits (tests/test_gpu_ops.py).
+// persistent grid; variant 0 = per layer (when N is a multiple of 128: the
+// operand-swapped kernel without a residual, or its CTA-pair form there with
+// TC_GEMM_TN_PAIR=1, and with a residual behind K >= 2048; else the single-CTA
+// kernel), 1 = single CTA, 2 = CTA pair, 3 = operand-swapped, 4 =
+// operand-swapped pair. The operand-swapped kernels give the single-CTA
+// kernel's bits (tests/test_gpu_ops.py).
 // Throws std::runtime_error on unsupported shapes.
 void launch_gemm(const GemmArgs &p, const __nv_bfloat16 *A, int lda, const __nv_bfloat16 *W, cudaStream_t st,
                  int bn = 0, int max_ctas = 0, int variant = 0);

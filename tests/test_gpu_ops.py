@@ -90,7 +90,7 @@ GEMM_SHAPES = [
 ]
 
 
-@pytest.mark.parametrize("variant", [1, 2, 3])
+@pytest.mark.parametrize("variant", [1, 2, 3, 4])
 @pytest.mark.parametrize("M,N,K", GEMM_SHAPES)
 @pytest.mark.parametrize("mode", ["bias", "bias_relu", "bias_res"])
 def test_gemm(lib, M, N, K, mode, variant):
@@ -388,18 +388,22 @@ def test_gemm_layernorm_fused(lib, M, K):
 
 
 @pytest.mark.parametrize("M,N,K,mode", [(20000, 640, 2560, "res"), (4099, 640, 640, "relu"), (300, 2560, 640, "bias"),
-                                        (1, 128, 2560, "bias"), (4099, 640, 640, "res"), (77, 1920, 640, "res")])
+                                        (1, 128, 2560, "bias"), (4099, 640, 640, "res"), (77, 1920, 640, "res"),
+                                        (5000, 1920, 640, "relu"), (77, 1920, 640, "bias")])
 def test_gemm_swapped_agrees_with_single(lib, M, N, K, mode):
-    """The operand-swapped kernel computes every output from the same products
-    in the same k order as the single-CTA kernel, so the two are bit-identical
-    (ragged last token tiles included), and both meet the GEMM tolerance."""
+    """The operand-swapped kernel and its CTA-pair form (which runs layers
+    without a residual; with one it falls back to the swapped kernel) compute
+    every output from the same products in the same k order as the single-CTA
+    kernel, so all three are bit-identical (ragged last token tiles and an
+    odd number of 128-feature blocks included), and they meet the GEMM
+    tolerance."""
     g = torch.Generator(device="cuda").manual_seed(M + N + K)
     A = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
     W = (torch.randn(N, K, device="cuda", generator=g) / K ** 0.5).to(torch.bfloat16)
     bias = torch.randn(N, device="cuda", generator=g) * 0.1
     res = torch.randn(M, N, device="cuda", generator=g).to(torch.bfloat16) if mode == "res" else None
     outs = []
-    for variant in (1, 3):
+    for variant in (1, 3, 4):
         out = torch.full((M, N), float("nan"), device="cuda", dtype=torch.bfloat16)
         status = torch.zeros(1, dtype=torch.int32, device="cuda")
         assert lib.tcb_op_gemm(_p(A), K, _p(W), _p(bias), int(mode == "relu"), _p(res), N, None, 1, None, None, _p(out),
@@ -409,6 +413,7 @@ def test_gemm_swapped_agrees_with_single(lib, M, N, K, mode):
         outs.append(out)
     ref, mag = gemm_ref(A, W, bias, mode == "relu", res)
     check_bf16(outs[0], ref, mag)
-    same = (outs[0].view(torch.int16) == outs[1].view(torch.int16)).float().mean().item()
-    print("bit-identical fraction", same)
-    assert same == 1.0
+    for other in outs[1:]:
+        same = (outs[0].view(torch.int16) == other.view(torch.int16)).float().mean().item()
+        print("bit-identical fraction", same)
+        assert same == 1.0

@@ -1,11 +1,13 @@
 """Opt-in kernel variants, each in a subprocess with its environment switch
-(the library reads TC_ATTN_TC, TC_LN_FUSE and TC_GEMM_VARIANT once at load):
+(the library reads TC_ATTN_TC, TC_LN_FUSE, TC_GEMM_VARIANT and TC_GEMM_TN_PAIR once at load):
 whole-tile parity against the oracle golden for the mma.sync attention on
 every chunk (TC_ATTN_TC=0), the tcgen05
 attention on every chunk of series up to 128 steps, short ones included
 (TC_ATTN_TC=2), the single-CTA GEMM on every layer (TC_GEMM_VARIANT=1), the
-operand-swapped GEMM on every layer it takes (=3), the LayerNorm-fused GEMM
-epilogue and the CTA-pair (cta_group::2) GEMM."""
+operand-swapped GEMM on every layer it takes (=3), its CTA-pair form on every
+layer without a residual (=4), the per-layer choice with that pair form
+(TC_GEMM_TN_PAIR=1), the LayerNorm-fused GEMM epilogue and the CTA-pair
+(cta_group::2) GEMM."""
 import os
 import subprocess
 import sys
@@ -35,7 +37,7 @@ assert_acceptance(m)
 
 
 @pytest.mark.parametrize("env", [{"TC_ATTN_TC": "0"}, {"TC_ATTN_TC": "2"}, {"TC_GEMM_VARIANT": "1"},
-                                 {"TC_GEMM_VARIANT": "3"},
+                                 {"TC_GEMM_VARIANT": "3"}, {"TC_GEMM_VARIANT": "4"}, {"TC_GEMM_TN_PAIR": "1"},
                                  {"TC_LN_FUSE": "1"}, {"TC_GEMM_VARIANT": "2"}])
 def test_variant_parity(env):
     code = CODE.format(pkg=str(REPO / "tessera-inference_b200"), orc=str(REPO / "oracle"), tests=str(REPO / "tests"))
