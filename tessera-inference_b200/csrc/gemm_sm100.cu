@@ -443,7 +443,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 //   bias is one value per lane; the residual block (32 tokens x 32 features)
 //   is loaded row-wise (8 rows x 64 B per instruction) into the staging
 //   buffer and read back by column; the bf16 results are written by column
-//   and stored by row, so global accesses stay 64-byte row segments.
+//   into the staging buffer, which one bulk tensor store per 32 x 32 block
+//   writes to global memory row by row.
 // Staging rows are 64 B with 16-byte chunks XOR-swizzled by (row >> 1) & 3,
 // which keeps both the row-wise and the column-wise accesses conflict-free.
 constexpr int TN_BM = 128, TN_BN = 256;  // features x tokens per tile
